@@ -1,0 +1,6 @@
+// Single translation unit for libb2attn.so: the device error record is one
+// __device__ symbol shared by every kernel, without relocatable device code.
+#include "api.cu"
+#include "decode.cu"
+#include "rope_append.cu"
+#include "prefill.cu"

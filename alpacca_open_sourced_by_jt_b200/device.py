@@ -1,0 +1,238 @@
+"""Device-tensor API over libb2attn.so.
+
+PyTorch is only the carrier here: tensors supply device pointers, the
+current CUDA stream and (outside this module) allocation.  Every function
+validates shapes/dtypes on the host, then makes one C-ABI call; nothing here
+synchronises, so the calls can be captured into a CUDA graph as long as the
+caller supplies `out` and `workspace` buffers (the library never allocates).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
+
+
+def _code(dtype: torch.dtype) -> int:
+    try:
+        return _DT[dtype]
+    except KeyError:
+        raise _lib.B2AShapeError(_lib.ERR_DTYPE, f"unsupported dtype {dtype}") from None
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream=None):
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def _need(cond: bool, msg: str):
+    if not cond:
+        raise _lib.B2AShapeError(_lib.ERR_SHAPE, msg)
+
+
+def _cuda_contig(name: str, t: torch.Tensor):
+    _need(t.is_cuda, f"{name} must be a CUDA tensor")
+    _need(t.is_contiguous(), f"{name} must be contiguous")
+
+
+# ---------------------------------------------------------------------------
+# decode
+# ---------------------------------------------------------------------------
+
+def decode_split_rows(batch: int, n_kv: int, max_len: int, kv_dtype: torch.dtype) -> int:
+    return int(_lib.load().b2a_decode_split_rows(batch, n_kv, max_len, _code(kv_dtype)))
+
+
+def decode_workspace_bytes(batch: int, n_head: int, head_dim: int, max_len: int,
+                           split_rows: int) -> int:
+    return int(_lib.load().b2a_decode_workspace_bytes(batch, n_head, head_dim, max_len,
+                                                      split_rows))
+
+
+def decode_workspace(batch: int, n_head: int, head_dim: int, max_len: int, split_rows: int,
+                     device) -> torch.Tensor:
+    """Allocate (via torch) a workspace big enough for b2a_decode."""
+    n = decode_workspace_bytes(batch, n_head, head_dim, max_len, split_rows)
+    return torch.empty(max(n, 16), dtype=torch.uint8, device=device)
+
+
+def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, lens: torch.Tensor,
+           *, scale: float | None = None, max_len: int | None = None, out=None, lse=None,
+           workspace=None, split_rows: int = 0, stream=None) -> torch.Tensor:
+    """Split-KV GQA decode.
+
+    q (B, H, D) f32; k_cache/v_cache (B, n_ctx, KV, D) or (n_ctx, KV, D) for
+    B == 1, dtype f32/f16/bf16 (sequence stride may exceed n_ctx*KV*D: pass a
+    view whose stride(0) is the stride); lens (B,) int32 on the device.
+    max_len bounds every lens entry (default n_ctx).  Returns out (B, H, D)
+    f32; lse (B, H) f32 receives the natural-log log-sum-exp if given.
+    """
+    if k_cache.dim() == 3:
+        k_cache = k_cache.unsqueeze(0)
+        v_cache = v_cache.unsqueeze(0)
+    _need(q.dim() == 3 and q.dtype == torch.float32 and q.is_cuda and q.is_contiguous(),
+          "q must be a contiguous CUDA f32 tensor (B, H, D)")
+    B, H, D = q.shape
+    _need(k_cache.dim() == 4 and k_cache.shape == v_cache.shape, "k_cache/v_cache shape mismatch")
+    _need(k_cache.dtype == v_cache.dtype, "k_cache/v_cache dtype mismatch")
+    Bc, n_ctx, KV, Dc = k_cache.shape
+    _need(Bc == B and Dc == D, f"cache {tuple(k_cache.shape)} does not match q {tuple(q.shape)}")
+    _need(k_cache[0].is_contiguous() and v_cache[0].is_contiguous(),
+          "each sequence's cache block must be contiguous")
+    _need(k_cache.stride(0) == v_cache.stride(0), "k/v caches need the same sequence stride")
+    _need(lens.dtype == torch.int32 and lens.is_cuda and lens.numel() == B,
+          "lens must be a CUDA int32 tensor (B,)")
+    seq_stride = k_cache.stride(0) if B > 1 else n_ctx * KV * D
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if max_len is None:
+        max_len = n_ctx
+    if split_rows <= 0:
+        split_rows = decode_split_rows(B, KV, max_len, k_cache.dtype)
+    if out is None:
+        out = torch.empty((B, H, D), dtype=torch.float32, device=q.device)
+    if workspace is None:
+        workspace = decode_workspace(B, H, D, max_len, split_rows, q.device)
+    if lse is not None:
+        _need(lse.dtype == torch.float32 and lse.numel() == B * H, "lse must be f32 (B, H)")
+    _lib.check(_lib.load().b2a_decode(
+        _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(lens), _ptr(out), _ptr(lse), _ptr(workspace),
+        workspace.numel() * workspace.element_size(), B, H, KV, D, n_ctx, seq_stride,
+        _code(k_cache.dtype), float(scale), int(max_len), int(split_rows), _stream(stream)))
+    return out
+
+
+def lse_combine(o_parts: torch.Tensor, lse_parts: torch.Tensor, *, out=None, lse=None,
+                stream=None) -> torch.Tensor:
+    """Merge G normalised partial outputs (G, R, D) by their lse (G, R)."""
+    _cuda_contig("o_parts", o_parts)
+    _cuda_contig("lse_parts", lse_parts)
+    G, R, D = o_parts.shape
+    _need(lse_parts.shape == (G, R), "lse_parts must be (G, R)")
+    if out is None:
+        out = torch.empty((R, D), dtype=torch.float32, device=o_parts.device)
+    _lib.check(_lib.load().b2a_lse_combine(_ptr(o_parts), _ptr(lse_parts), G, R, D, _ptr(out),
+                                           _ptr(lse), _stream(stream)))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# prefill
+# ---------------------------------------------------------------------------
+
+def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, positions: torch.Tensor, *,
+            scale: float | None = None, window: int = 0, kv_start: int = 0,
+            out_dtype: torch.dtype | None = None, out=None, stream=None) -> torch.Tensor:
+    """Causal flash prefill on tcgen05.
+
+    q (T, H, D) f16/bf16; k, v (t_kv, KV, D) same dtype (the cache rows
+    kv_start..kv_start+t_kv-1); positions (T,) int32 absolute positions.
+    Returns (T, H, D) in out_dtype (default q.dtype)."""
+    for n_, t_ in (("q", q), ("k", k), ("v", v), ("positions", positions)):
+        _cuda_contig(n_, t_)
+    _need(q.dim() == 3 and k.dim() == 3 and k.shape == v.shape, "q (T,H,D), k/v (t_kv,KV,D)")
+    _need(q.dtype == k.dtype == v.dtype and q.dtype in (torch.float16, torch.bfloat16),
+          "q/k/v must share dtype f16 or bf16")
+    T, H, D = q.shape
+    t_kv, KV, Dk = k.shape
+    _need(Dk == D, "head_dim mismatch")
+    _need(positions.dtype == torch.int32 and positions.numel() == T, "positions int32 (T,)")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty((T, H, D), dtype=out_dtype or q.dtype, device=q.device)
+    _lib.check(_lib.load().b2a_prefill(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(positions), _ptr(out), T, t_kv, H, KV, D,
+        _code(q.dtype), _code(out.dtype), float(scale), int(window), int(kv_start),
+        _stream(stream)))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# RoPE + append
+# ---------------------------------------------------------------------------
+
+_STYLE = {"norm": _lib.ROPE_NORM, "neox": _lib.ROPE_NEOX}
+
+
+def rope_append(q: torch.Tensor, k: torch.Tensor | None, v: torch.Tensor | None,
+                positions: torch.Tensor, cos_tab: torch.Tensor, sin_tab: torch.Tensor, *,
+                k_cache=None, v_cache=None, n_rot: int | None = None, style: str = "norm",
+                per_sequence: bool = False, q_out=None, bq=None, bk=None, bv=None,
+                stream=None):
+    """Fused bias + RoPE + KV append for n tokens.
+
+    q (n, H, D) f32 (rotated in place unless q_out is given); k, v (n, KV, D)
+    f32 rows or None (rope-only); positions (n,) int32; caches (S, n_ctx, KV,
+    D) or (n_ctx, KV, D).  per_sequence=True puts token i in sequence i
+    (batched decode), else all tokens in sequence 0 (a prefill chunk).
+    Returns the tensor holding the rotated q."""
+    _need(q.dim() == 3 and q.dtype == torch.float32 and q.is_cuda, "q must be CUDA f32 (n,H,D)")
+    n, H, D = q.shape
+    _need(q.stride(2) == 1 and q.stride(1) == D, "q rows must be contiguous per token")
+    _need(positions.dtype == torch.int32 and positions.is_cuda and positions.numel() == n,
+          "positions int32 (n,)")
+    _cuda_contig("cos_tab", cos_tab)
+    _cuda_contig("sin_tab", sin_tab)
+    if n_rot is None:
+        n_rot = 2 * cos_tab.shape[1]
+    _need(cos_tab.shape[1] * 2 == n_rot, "cos table width must be n_rot/2")
+    KV, seq_stride, n_ctx, kv_dt = 0, 0, cos_tab.shape[0], _lib.F32
+    ks = vs = 0
+    if k is not None:
+        _need(k_cache is not None and v_cache is not None, "k/v given without caches")
+        if k_cache.dim() == 3:
+            k_cache, v_cache = k_cache.unsqueeze(0), v_cache.unsqueeze(0)
+        _need(k_cache.shape == v_cache.shape and k_cache.dtype == v_cache.dtype, "cache mismatch")
+        _, n_ctx, KV, Dc = k_cache.shape
+        _need(Dc == D and k.shape == (n, KV, D) and v.shape == (n, KV, D), "k/v shape")
+        _need(k.stride(2) == 1 and v.stride(2) == 1 and k.stride(1) == D and v.stride(1) == D,
+              "k/v rows must be contiguous per token")
+        seq_stride = k_cache.stride(0)
+        kv_dt = _code(k_cache.dtype)
+        ks, vs = k.stride(0), v.stride(0)
+    qo_dt = _lib.F32
+    if q_out is not None:
+        _cuda_contig("q_out", q_out)
+        qo_dt = _code(q_out.dtype)
+    _lib.check(_lib.load().b2a_rope_append(
+        _ptr(q), q.stride(0), _ptr(k), ks, _ptr(v), vs, _ptr(bq), _ptr(bk), _ptr(bv),
+        _ptr(cos_tab), _ptr(sin_tab), cos_tab.shape[0], _ptr(positions), int(per_sequence),
+        _ptr(k_cache), _ptr(v_cache), seq_stride, n_ctx, kv_dt, _ptr(q_out), qo_dt, n, H, KV, D,
+        int(n_rot), _STYLE[style], _stream(stream)))
+    return q if q_out is None else q_out
+
+
+def imrope_append(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, lanes: torch.Tensor,
+                  positions: torch.Tensor, sections, *, k_cache, v_cache, freq_base: float,
+                  freq_scale: float = 1.0, per_sequence: bool = False, q_out=None,
+                  stream=None) -> torch.Tensor:
+    """Qwen35 IMROPE of q/k plus KV append.  lanes (n, 4) int32 position
+    lanes; sections 4 ints; positions (n,) cache rows.  Returns q_out."""
+    _need(q.dim() == 3 and q.dtype == torch.float32 and q.is_cuda, "q must be CUDA f32 (n,H,D)")
+    n, H, D = q.shape
+    if k_cache.dim() == 3:
+        k_cache, v_cache = k_cache.unsqueeze(0), v_cache.unsqueeze(0)
+    _, n_ctx, KV, _ = k_cache.shape
+    for n_, t_ in (("q", q), ("k", k), ("v", v), ("lanes", lanes), ("positions", positions)):
+        _cuda_contig(n_, t_)
+    _need(lanes.dtype == torch.int32 and lanes.shape == (n, 4), "lanes int32 (n, 4)")
+    if q_out is None:
+        q_out = torch.empty_like(q)
+    import ctypes
+    sec = (ctypes.c_int * 4)(*[int(s) for s in sections])
+    _lib.check(_lib.load().b2a_imrope_append(
+        _ptr(q), H * D, _ptr(k), KV * D, _ptr(v), KV * D, _ptr(lanes), sec, float(freq_base),
+        float(freq_scale), _ptr(positions), int(per_sequence), _ptr(k_cache), _ptr(v_cache),
+        k_cache.stride(0), n_ctx, _code(k_cache.dtype), _ptr(q_out), _code(q_out.dtype), n, H,
+        KV, D, _stream(stream)))
+    return q_out

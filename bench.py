@@ -1,0 +1,461 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention path (one JSON line on stdout, rank 0).
+
+Headline (`value`): split-KV decode attention at 32K context, the workload
+the reference's metric is quoted on ("decode-attn KV GB/s @32K ctx"):
+batch 16 sequences x 32768 cached tokens, 32 query / 8 KV heads, head_dim
+128, bf16 KV ~ N(0,1) (seed 4 + rank).  One step = one b2a_decode call over
+the whole batch (split kernel + combine kernel).  value = algorithmic KV
+bytes (B*2*L*KV*D*2 per rank, all ranks) / max-over-ranks device time.
+The caches (2.15 GB per rank) exceed the 126 MB L2, so no flush is needed.
+
+Also reported on the same line:
+  prefill   BASELINE config 2 causal prefill (S=2048, 32/8 heads, D=128,
+            bf16 in/out) in TFLOP/s, flops = 4*H*D*S(S+1)/2, L2 flushed
+            between launches (inputs are 24 MB)
+  e2e       the decode step through the public API with host buffers: per
+            step the pinned host q/k/v rows of the new token go H2D, the
+            fused RoPE+append writes them into the resident cache, decode
+            runs, the output comes back D2H and the host waits for it
+  roofline  decode against MEASURED_PEAKS.json's copy bandwidth
+  cpu_baseline  the reference's NumPy decode (oracle port) on host cores
+
+Multi-GPU (torchrun, one rank per GPU): every rank decodes its own batch of
+16 sequences (sequence sharding, no collective on the data path), so
+scaling is weak; timing is the max over ranks of CUDA-event time.
+
+`--impl reference` times the reference's CPU implementation (the NumPy
+restatement in oracle/, the reference itself being Python that does not
+travel to the GPU box) on the same workload definition, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "decode-attn KV GB/s (% HBM peak) @32K ctx; prefill-attn TFLOPS; at 1/2/4/8 GPU"
+WL = dict(B=16, L=32768, H=32, KV=8, D=128)            # decode workload (per rank)
+PF = dict(S=2048, H=32, KV=8, D=128)                   # prefill workload (config 2)
+FALLBACK_HBM = 6650.0
+FALLBACK_BF16 = 1590.0
+SPEC_HBM = 8000.0
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def decode_bytes(B, L, KV, D, elem=2):
+    return B * 2 * L * KV * D * elem
+
+
+def prefill_flops(S, H, D):
+    return 4 * H * D * S * (S + 1) / 2
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return (float(j["hbm_gbs"]), float(j["bf16_tflops"]),
+                float(j.get("bf16_tflops_sustained", j["bf16_tflops"])), "measured")
+    except Exception:
+        return FALLBACK_HBM, FALLBACK_BF16, 1400.0, "fallback"
+
+
+def profiled_traffic(name):
+    """Per-launch DRAM traffic recorded from an ncu capture in profiles/."""
+    p = os.path.join(REPO, "profiles", "traffic.md")
+    try:
+        for line in open(p):
+            if line.startswith(f"| {name} |"):
+                return float(line.split("|")[2].strip())
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", self.gpu_id], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.2)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gpu_id_for(dev_index):
+    import torch
+    try:
+        u = str(torch.cuda.get_device_properties(dev_index).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        return vis.split(",")[dev_index] if vis else str(dev_index)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def bench_decode(dev, rank, steps, warmup, dist):
+    import torch
+    from alpacca_open_sourced_by_jt_b200 import device
+    B, L, H, KV, D = WL["B"], WL["L"], WL["H"], WL["KV"], WL["D"]
+    g = torch.Generator(device=dev).manual_seed(4 + rank)
+    kc = torch.randn((B, L, KV, D), device=dev, dtype=torch.bfloat16, generator=g)
+    vc = torch.randn((B, L, KV, D), device=dev, dtype=torch.bfloat16, generator=g)
+    q = torch.randn((B, H, D), device=dev, dtype=torch.float32, generator=g)
+    lens = torch.full((B,), L, dtype=torch.int32, device=dev)
+    split = device.decode_split_rows(B, KV, L, torch.bfloat16)
+    ws = device.decode_workspace(B, H, D, L, split, dev)
+    out = torch.empty((B, H, D), dtype=torch.float32, device=dev)
+
+    def step():
+        device.decode(q, kc, vc, lens, out=out, workspace=ws, split_rows=split, max_len=L)
+
+    for _ in range(max(warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    return dict(ms=ms, split=split, kc=kc, vc=vc, q=q, lens=lens, ws=ws, out=out)
+
+
+def bench_e2e(dev, st, steps, warmup):
+    """Decode step through the public API with host buffers (see module doc)."""
+    import numpy as np
+    import torch
+    import oracle
+    from alpacca_open_sourced_by_jt_b200 import device
+    B, L, H, KV, D = WL["B"], WL["L"], WL["H"], WL["KV"], WL["D"]
+    cos, sin = oracle.rope_tables(L, D, 500000.0)
+    ct, stt = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+    rng = np.random.default_rng(7)
+    h_q = torch.from_numpy(rng.standard_normal((B, H, D), dtype=np.float32)).pin_memory()
+    h_k = torch.from_numpy(rng.standard_normal((B, KV, D), dtype=np.float32)).pin_memory()
+    h_v = torch.from_numpy(rng.standard_normal((B, KV, D), dtype=np.float32)).pin_memory()
+    h_out = torch.empty((B, H, D), dtype=torch.float32).pin_memory()
+    d_q = torch.empty_like(h_q, device=dev)
+    d_k = torch.empty_like(h_k, device=dev)
+    d_v = torch.empty_like(h_v, device=dev)
+    pos = torch.full((B,), L - 1, dtype=torch.int32, device=dev)
+    kc, vc, lens, ws, out, split = st["kc"], st["vc"], st["lens"], st["ws"], st["out"], st["split"]
+
+    def step():
+        d_q.copy_(h_q, non_blocking=True)
+        d_k.copy_(h_k, non_blocking=True)
+        d_v.copy_(h_v, non_blocking=True)
+        device.rope_append(d_q, d_k, d_v, pos, ct, stt, k_cache=kc, v_cache=vc,
+                           per_sequence=True)
+        device.decode(d_q, kc, vc, lens, out=out, workspace=ws, split_rows=split, max_len=L)
+        h_out.copy_(out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(max(warmup, 3)):
+        step()
+    n = max(3, min(steps, 500))
+    t0 = time.perf_counter()
+    for _ in range(n):
+        step()
+    dt = time.perf_counter() - t0
+    bytes_step = decode_bytes(B, L, KV, D)
+    return dict(value=bytes_step / (dt / n) / 1e9, unit="GB/s",
+                h2d_bytes_per_step=int(h_q.numel() * 4 + h_k.numel() * 4 + h_v.numel() * 4),
+                d2h_bytes_per_step=int(h_out.numel() * 4), steps=n,
+                ms_per_step=dt / n * 1e3,
+                path="rope_append + decode with resident cache, pinned host q/k/v in, out back")
+
+
+def bench_prefill(dev, steps, warmup):
+    import torch
+    from alpacca_open_sourced_by_jt_b200 import device
+    S, H, KV, D = PF["S"], PF["H"], PF["KV"], PF["D"]
+    g = torch.Generator(device=dev).manual_seed(1)
+    q = torch.randn((S, H, D), device=dev, dtype=torch.bfloat16, generator=g)
+    k = torch.randn((S, KV, D), device=dev, dtype=torch.bfloat16, generator=g)
+    v = torch.randn((S, KV, D), device=dev, dtype=torch.bfloat16, generator=g)
+    pos = torch.arange(S, dtype=torch.int32, device=dev)
+    out = torch.empty((S, H, D), dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def call():
+        device.prefill(q, k, v, pos, out=out)
+
+    for _ in range(max(warmup, 3)):
+        call()
+    n = max(5, min(steps, 200))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(n)]
+    torch.cuda.synchronize()
+    for a, b in evs:
+        flush.zero_()
+        a.record()
+        call()
+        b.record()
+    torch.cuda.synchronize()
+    times = [a.elapsed_time(b) for a, b in evs]
+    ms = sum(times) / n
+    fl = prefill_flops(S, H, D)
+    return dict(ms=ms, tflops=fl / (ms * 1e-3) / 1e12, launches=n, q=q, k=k, v=v)
+
+
+def cpu_decode_baseline(st, budget_s=10.0):
+    import numpy as np
+    import oracle
+    L, H, KV, D = WL["L"], WL["H"], WL["KV"], WL["D"]
+    K = st["kc"][0].float().cpu().numpy()
+    V = st["vc"][0].float().cpu().numpy()
+    q = st["q"][0].cpu().numpy()
+    oracle.attention_decode(q, K, V, H // KV, 1 / math.sqrt(D))
+    n, t0 = 0, time.perf_counter()
+    while n < 3 or time.perf_counter() - t0 < budget_s:
+        oracle.attention_decode(q, K, V, H // KV, 1 / math.sqrt(D))
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return {"value": decode_bytes(1, L, KV, D) / dt / 1e9, "unit": "GB/s",
+            "cores": os.cpu_count(), "kind": "port",
+            "sample": f"1 of the 16 sequences (32768 x 8 KV heads x 128, fp32 NumPy, the "
+                      f"reference's _attention_np restated), {n} calls, {dt*1e3:.1f} ms each; "
+                      f"GB/s counts the workload's bf16 KV bytes"}
+
+
+def cpu_prefill_baseline(pf):
+    import oracle
+    S, H, KV, D = PF["S"], PF["H"], PF["KV"], PF["D"]
+    g = H // KV
+    q = pf["q"][:, :g].float().cpu().numpy()
+    k = pf["k"][:, :1].float().cpu().numpy()
+    v = pf["v"][:, :1].float().cpu().numpy()
+    import numpy as np
+    pos = np.arange(S, dtype=np.int32)
+    t0 = time.perf_counter()
+    oracle.attention_batch(q, k, v, pos, g, 1 / math.sqrt(D))
+    dt = time.perf_counter() - t0
+    return {"value": prefill_flops(S, g, D) / dt / 1e12, "unit": "TFLOP/s",
+            "cores": os.cpu_count(), "kind": "port",
+            "sample": f"1 of 8 KV heads (4 query heads) of config 2 through the reference's "
+                      f"_attention_batch_np einsum path restated, {dt:.2f} s"}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as tdist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    from alpacca_open_sourced_by_jt_b200 import build as _b
+    if rank == 0 and not _b.up_to_date():
+        _b.build()
+    dist = None
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                 device_id=torch.device("cuda", local))
+        dist = tdist
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from alpacca_open_sourced_by_jt_b200 import _lib
+    _lib.load()
+    _lib.device_error(clear=True)
+
+    clocks = ClockSampler(gpu_id_for(local)) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    st = bench_decode(dev, rank, args.steps, args.warmup, dist)
+    clk = clocks.stop() if clocks else None
+    ms = st["ms"]
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        ms = float(t.item())
+    B, L, KV, D = WL["B"], WL["L"], WL["KV"], WL["D"]
+    per_step = decode_bytes(B, L, KV, D)
+    value = world * per_step * args.steps / (ms * 1e-3) / 1e9
+    hbm, bf16, bf16_sus, src = peaks()
+    achieved = per_step / (ms / args.steps * 1e-3) / 1e9   # per rank, per launch pair
+    result = None
+    if rank == 0:
+        e2e = bench_e2e(dev, st, args.steps, args.warmup)
+        e2e["value"] *= world
+        pf = bench_prefill(dev, args.steps, args.warmup) if not args.no_prefill else None
+        _lib.raise_device_error()
+        cpu = cpu_decode_baseline(st) if (world == 1 and not args.no_cpu_baseline) else None
+        traffic = profiled_traffic("decode_mma_kernel bf16 D128 NT1")
+        result = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "decode@32K: 16 seqs x 32768 ctx, 32 q / 8 KV heads, "
+                                   "head_dim 128, bf16 KV ~N(0,1), 1 query token per seq",
+                       "batch_per_gpu": B, "ctx": L, "q_heads": WL["H"], "kv_heads": KV,
+                       "head_dim": D, "split_rows": st["split"],
+                       "l2": "caches 2.15 GB per GPU > 126 MB L2; no flush",
+                       "parallelism": f"sequence-sharded x{world} (no collective)"},
+            "hbm_frac_of_spec": round(value / world / SPEC_HBM, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                         "traffic": traffic, "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)",
+                         "kernel": "decode_mma_kernel<bf16,128,1> + decode_combine_kernel, "
+                                   "timed together per b2a_decode call"},
+            "gpu_launches": 2 * args.steps,
+            "e2e": e2e,
+        }
+        if cpu:
+            result["cpu_baseline"] = cpu
+        if clk:
+            result["clocks"] = clk
+        if pf:
+            pcpu = cpu_prefill_baseline(pf) if (world == 1 and not args.no_cpu_baseline) else None
+            result["prefill"] = {
+                "metric": "prefill-attn TFLOPS", "value": round(pf["tflops"], 1),
+                "unit": "TFLOP/s", "ms_per_launch": round(pf["ms"], 4),
+                "config": "BASELINE config 2: S=2048 causal, 32 q / 8 KV heads, D=128, bf16 "
+                          "in/out, fp32 accumulation; L2 flushed before each launch",
+                "roofline": {"bound": "tensor", "achieved": round(pf["tflops"], 1),
+                             "peak": bf16, "unit": "TFLOP/s",
+                             "frac": round(pf["tflops"] / bf16, 4),
+                             "traffic": profiled_traffic("prefill_kernel bf16 D128"),
+                             "peak_source": f"{src} (MEASURED_PEAKS.json bf16_tflops, burst)"},
+                "launches": pf["launches"]}
+            if pcpu:
+                result["prefill"]["cpu_baseline"] = pcpu
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+    import oracle
+    L, H, KV, D = WL["L"], WL["H"], WL["KV"], WL["D"]
+    rng = np.random.default_rng(4)
+    q = rng.standard_normal((H, D), dtype=np.float32)
+    K = rng.standard_normal((L, KV, D), dtype=np.float32)
+    V = rng.standard_normal((L, KV, D), dtype=np.float32)
+    # calibrate: keep the whole W + K run near a minute of CPU time
+    t0 = time.perf_counter()
+    oracle.attention_decode(q, K, V, H // KV, 1 / math.sqrt(D))
+    t_full = time.perf_counter() - t0
+    per_step_budget = 60.0 / max(1, args.steps + args.warmup)
+    rows = int(min(L, max(1024, L * per_step_budget / max(t_full, 1e-6))))
+    Ks, Vs = np.ascontiguousarray(K[:rows]), np.ascontiguousarray(V[:rows])
+    for _ in range(args.warmup):
+        oracle.attention_decode(q, Ks, Vs, H // KV, 1 / math.sqrt(D))
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.attention_decode(q, Ks, Vs, H // KV, 1 / math.sqrt(D))
+    dt = (time.perf_counter() - t0) / args.steps
+    value = decode_bytes(1, rows, KV, D) / dt / 1e9
+    sample = (f"each step: one sequence's decode over {rows} of its 32768 cached rows "
+              f"(32 q / 8 KV heads, D=128, fp32 NumPy, the reference's _attention_np "
+              f"restated); GB/s counts the workload's bf16 KV bytes")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "decode@32K (per-sequence sample)", "ctx": L, "q_heads": H,
+                   "kv_heads": KV, "head_dim": D, "rows_per_step": rows},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": os.cpu_count(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

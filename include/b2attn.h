@@ -1,0 +1,176 @@
+/*
+ * b2attn.h - C ABI of libb2attn.so, the B200 (sm_100a) attention path for the
+ * alpaccaroo inference engine.
+ *
+ * Three hot kernels sit behind this boundary:
+ *   1. single-token GQA decode over the KV cache with split-KV partitions and
+ *      a log-sum-exp combine           (b2a_decode, b2a_lse_combine)
+ *   2. causal flash prefill on tcgen05 tensor cores with TMEM accumulators
+ *                                      (b2a_prefill)
+ *   3. fused RoPE (norm / neox / IMROPE) plus KV-cache append
+ *                                      (b2a_rope_append, b2a_imrope_append)
+ *
+ * Conventions (all entry points):
+ *   - Every pointer named *_dev, and every tensor argument, is device memory
+ *     on the current CUDA device; `stream` is a cudaStream_t (NULL = legacy
+ *     default stream).  Nothing here allocates device memory, synchronises
+ *     the stream or reads device memory on the host, so every call can be
+ *     captured into a CUDA graph.  Lengths and positions that change from
+ *     token to token are read from device buffers for the same reason.
+ *   - The KV cache keeps the reference layout: per layer and per sequence a
+ *     token-major [n_ctx][n_kv][head_dim] block (alpaccaroo/model.py:867-870),
+ *     rows addressed by absolute position.  A batch of sequences is a set of
+ *     such blocks `seq_stride` elements apart.
+ *   - Return value: B2A_OK (0) or a B2A_ERR_* code; b2a_last_error() holds a
+ *     message for the calling thread.  Kernels never trap: a bounded device
+ *     wait that expires or a position outside the cache records a code that
+ *     b2a_device_error() reads back.
+ */
+#ifndef B2ATTN_H_
+#define B2ATTN_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2A_ABI_VERSION 1
+
+/* element types */
+#define B2A_F32 0
+#define B2A_F16 1
+#define B2A_BF16 2
+
+/* RoPE styles (alpaccaroo/model.py:1162-1209: "norm" adjacent pairs, "neox"
+ * split halves) */
+#define B2A_ROPE_NORM 0
+#define B2A_ROPE_NEOX 1
+
+/* status codes */
+#define B2A_OK 0
+#define B2A_ERR_ARG 1         /* null pointer, negative or zero size        */
+#define B2A_ERR_SHAPE 2       /* inconsistent shapes (heads, group, ...)     */
+#define B2A_ERR_DTYPE 3       /* unsupported element type combination       */
+#define B2A_ERR_ALIGN 4       /* pointer or stride not 16-byte aligned       */
+#define B2A_ERR_UNSUPPORTED 5 /* head_dim or group outside the kernels' set  */
+#define B2A_ERR_WORKSPACE 6   /* caller workspace too small                  */
+#define B2A_ERR_CUDA 7        /* CUDA runtime / driver error at launch       */
+#define B2A_ERR_TIMEOUT 8     /* device: a bounded wait expired              */
+#define B2A_ERR_POSITION 9    /* device: position outside cache or table     */
+
+/* ---- library ---------------------------------------------------------- */
+
+int b2a_version(void);
+const char* b2a_last_error(void);
+
+/* Read (and with clear != 0, reset) the device error record of the current
+ * device.  Synchronises the device.  *code = 0 means no kernel reported. */
+int b2a_device_error(int* code, int* aux, int clear);
+
+/* ---- (1) split-KV GQA decode ------------------------------------------
+ *
+ * Replaces Model._attention_np (alpaccaroo/model.py:1231-1252),
+ * kernels.attention_decode (alpaccaroo/kernels.py:1183-1200),
+ * qwen35_kernels.qwen35_full_attention_decode (qwen35_kernels.py:363-392) and
+ * the device pair _attention_decode_part/_attention_decode_combine
+ * (alpaccaroo/cuda.py:580-694, kernel table cuda.py:967-981).
+ *
+ *   q        f32 [B][H][D]        one query token per sequence
+ *   k_cache  kv_dtype, sequence b at k_cache + b*seq_stride, [n_ctx][KV][D]
+ *   v_cache  same layout as k_cache
+ *   lens_dev int32 [B]            logical length of each sequence (rows
+ *                                 0..len-1 are attended; 0 gives out = 0 and
+ *                                 lse = -inf)
+ *   out      f32 [B][H][D]        softmax(q.K^T * scale) . V
+ *   lse_out  f32 [B][H] or NULL   natural-log log-sum-exp of the scaled
+ *                                 scores, for b2a_lse_combine across shards
+ *   max_len  host upper bound on every lens_dev entry (<= n_ctx); sizes the
+ *            fixed launch grid so a captured graph replays for any lengths
+ *   split_rows  KV rows per CTA (multiple of 64), 0 = library choice
+ * Head h reads KV head h / (H / KV) (contiguous grouping, qwen35_ops.py:406-
+ * 472).  kv_dtype F16/BF16 runs the TMA + tensor-core kernel (D in {64, 128,
+ * 256}, H/KV <= 16); F32 runs an fp32 FMA kernel (D % 32 == 0, D <= 256). */
+size_t b2a_decode_workspace_bytes(int B, int H, int D, int max_len, int split_rows);
+int b2a_decode_split_rows(int B, int KV, int max_len, int kv_dtype);
+int b2a_decode(const float* q, const void* k_cache, const void* v_cache, const int* lens_dev,
+               float* out, float* lse_out, void* workspace, size_t workspace_bytes, int B, int H,
+               int KV, int D, int n_ctx, long long seq_stride, int kv_dtype, float scale,
+               int max_len, int split_rows, void* stream);
+
+/* Merge G partial decodes of the same queries over disjoint KV ranges (the
+ * long-context shard combine).  Same algebra as _attention_decode_combine
+ * (alpaccaroo/cuda.py:674-694) with normalised parts:
+ *   out[r] = sum_g exp(lse[g][r] - L) * o[g][r],  L = log sum_g exp(lse[g][r])
+ *   o_parts f32 [G][rows][D], lse_parts f32 [G][rows]; lse_out may be NULL. */
+int b2a_lse_combine(const float* o_parts, const float* lse_parts, int G, int rows, int D,
+                    float* out, float* lse_out, void* stream);
+
+/* ---- (2) causal prefill on tcgen05 --------------------------------------
+ *
+ * Replaces Model._attention_batch_np (alpaccaroo/model.py:1254-1272), its
+ * window variant _attention_batch_window_np (model.py:1567-1592),
+ * cuda.attention_batch / _attention_batch_gqa (alpaccaroo/cuda.py:424-578,
+ * 1186-1242) and qwen35_full_attention_prefill (qwen35_kernels.py:395-411).
+ *
+ *   q        in_dtype [T][H][D]   rotated queries (F16 or BF16)
+ *   k_cache  in_dtype [t_kv][KV][D] rows kv_start .. kv_start+t_kv-1
+ *   v_cache  same
+ *   pos_dev  int32 [T]            absolute position of each query token
+ *   out      out_dtype [T][H][D]  (F32, F16 or BF16)
+ * Key s (absolute position kv_start+s) is visible to query t iff
+ * kv_start+s <= pos[t] and (window <= 0 or kv_start+s > pos[t]-window).
+ * A query row with no visible key gets 0.  D must be 64 or 128. */
+int b2a_prefill(const void* q, const void* k_cache, const void* v_cache, const int* pos_dev,
+                void* out, int T, int t_kv, int H, int KV, int D, int in_dtype, int out_dtype,
+                float scale, int window, int kv_start, void* stream);
+
+/* ---- (3) fused RoPE + KV append ----------------------------------------
+ *
+ * Replaces _rope_np / _rope_batch_np plus the cache-row stores
+ * (alpaccaroo/model.py:1162-1209, 1331-1337, 1429-1432), kernels.rope_decode
+ * (kernels.py:1172-1180) and the device kernels _rope_store_decode /
+ * _rope_store_batch (alpaccaroo/cuda.py:723-786, 885-953).
+ *
+ * For each token i (0..n_tok-1) at position p = pos_dev[i]:
+ *   q row  q + i*q_tok_stride      [H][D] f32, plus bq if non-NULL, rotated;
+ *          written to q_out (+ i*H*D, q_out_dtype) or, if q_out is NULL, in
+ *          place into q
+ *   k row  k + i*k_tok_stride      [KV][D] f32 (+bk), rotated, stored at
+ *          k_cache row p of sequence s
+ *   v row  v + i*v_tok_stride      [KV][D] f32 (+bv), stored at v_cache row p
+ * where s = i if tok_seq_mode == 1 (batched decode: one token per sequence)
+ * and s = 0 if tok_seq_mode == 0 (a prefill chunk of one sequence).
+ * cos_tab / sin_tab are the engine's f32 tables [tab_rows][n_rot/2]
+ * (model.py:871-875); products and differences are rounded separately, so
+ * f32 results are bit-identical to the NumPy path.  Dims n_rot..D-1 pass
+ * through.  A position outside [0, min(n_ctx, tab_rows)) writes nothing and
+ * records B2A_ERR_POSITION.  KV = 0 (k, v and caches NULL) rotates q only,
+ * the contract of kernels.rope_decode. */
+int b2a_rope_append(float* q, long long q_tok_stride, const float* k, long long k_tok_stride,
+                    const float* v, long long v_tok_stride, const float* bq, const float* bk,
+                    const float* bv, const float* cos_tab, const float* sin_tab, int tab_rows,
+                    const int* pos_dev, int tok_seq_mode, void* k_cache, void* v_cache,
+                    long long seq_stride, int n_ctx, int kv_dtype, void* q_out, int q_out_dtype,
+                    int n_tok, int H, int KV, int D, int n_rot, int style, void* stream);
+
+/* IMROPE variant for the Qwen35 full-attention layers (qwen35_ops.py:138-215,
+ * qwen35_cuda.py:965-1008): pair j < sum(sections) rotates dims (j,
+ * j+sum(sections)) by theta = lanes[lane(j)] * freq_scale *
+ * freq_base^(-2j / (2*sum(sections))), lane(j) the interleaved T/H/W/E
+ * schedule, evaluated in double precision like the reference.
+ *   lanes_dev int32 [n_tok][4] position lanes ([p,p,p,0] for text)
+ *   sections  host int[4]
+ * Cache row, q/k/v and output arguments as in b2a_rope_append. */
+int b2a_imrope_append(const float* q, long long q_tok_stride, const float* k,
+                      long long k_tok_stride, const float* v, long long v_tok_stride,
+                      const int* lanes_dev, const int* sections, double freq_base,
+                      double freq_scale, const int* pos_dev, int tok_seq_mode, void* k_cache,
+                      void* v_cache, long long seq_stride, int n_ctx, int kv_dtype, void* q_out,
+                      int q_out_dtype, int n_tok, int H, int KV, int D, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2ATTN_H_ */

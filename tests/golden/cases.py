@@ -1,0 +1,112 @@
+"""Seeded input cases shared by the golden generator and the tests.
+
+Every case returns its arrays plus `sha256`, a digest of the input bytes, so
+a test can check that it regenerated exactly the inputs the golden file was
+made from.  Shapes follow BASELINE.json's configs (config 1 exactly; the
+others at sizes a CPU finishes in seconds).
+"""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+
+CONFIG1_SAMPLE_ROWS = (0, 1, 2, 63, 64, 255, 300, 510, 511)
+
+
+def _digest(*arrays) -> str:
+    h = hashlib.sha256()
+    for a in arrays:
+        a = np.ascontiguousarray(a)
+        h.update(str(a.dtype).encode())
+        h.update(str(a.shape).encode())
+        h.update(a.tobytes())
+    return h.hexdigest()
+
+
+def decode_config1():
+    """batch 1, 32 query / 8 KV heads, head_dim 64,
+    context 512, fp32, Q/K/V ~ N(0,1) seed 0, RoPE theta 500000 ("norm",
+    llama) on K positions 0..511 and q at 511, scale 1/sqrt(64)."""
+    H, KV, D, L = 32, 8, 64, 512
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((H, D), dtype=np.float32)
+    k = rng.standard_normal((L, KV, D), dtype=np.float32)
+    v = rng.standard_normal((L, KV, D), dtype=np.float32)
+    return dict(H=H, KV=KV, D=D, L=L, base=500000.0, q_raw=q, k_raw=k, v=v,
+                sha256=_digest(q, k, v))
+
+
+def rope_neox():
+    """Partial-rotary neox case: 4 q / 2 KV heads, head_dim 64, n_rot 32,
+    base 10000, six tokens at scattered positions."""
+    H, KV, D, n_rot, n_ctx = 4, 2, 64, 32, 256
+    rng = np.random.default_rng(11)
+    positions = np.array([0, 1, 5, 77, 128, 255], np.int32)
+    q = rng.standard_normal((len(positions), H, D), dtype=np.float32)
+    k = rng.standard_normal((len(positions), KV, D), dtype=np.float32)
+    return dict(H=H, KV=KV, D=D, n_rot=n_rot, n_ctx=n_ctx, base=10000.0, positions=positions,
+                q=q, k=k, sha256=_digest(q, k, positions))
+
+
+def prefill_small():
+    """Causal prefill chunk after a 13-token prefix: 37 queries at positions
+    13..49 over 50 keys, 8 q / 2 KV heads, head_dim 64, fp32 N(0,1)."""
+    H, KV, D, pre, t = 8, 2, 64, 13, 37
+    rng = np.random.default_rng(21)
+    q = rng.standard_normal((t, H, D), dtype=np.float32)
+    k = rng.standard_normal((pre + t, KV, D), dtype=np.float32)
+    v = rng.standard_normal((pre + t, KV, D), dtype=np.float32)
+    positions = np.arange(pre, pre + t, dtype=np.int32)
+    return dict(H=H, KV=KV, D=D, t_kv=pre + t, q=q, k=k, v=v, positions=positions,
+                sha256=_digest(q, k, v, positions))
+
+
+def prefill_window():
+    """Sliding-window variant (gemma3 semantics): window 16, kv_start 5."""
+    H, KV, D, t = 4, 2, 64, 40
+    rng = np.random.default_rng(22)
+    q = rng.standard_normal((t, H, D), dtype=np.float32)
+    k = rng.standard_normal((45, KV, D), dtype=np.float32)
+    v = rng.standard_normal((45, KV, D), dtype=np.float32)
+    positions = np.arange(10, 10 + t, dtype=np.int32)
+    return dict(H=H, KV=KV, D=D, window=16, kv_start=5, q=q, k=k, v=v, positions=positions,
+                sha256=_digest(q, k, v, positions))
+
+
+def qwen35_decode():
+    """Qwen35 full-attention decode: 8 q / 2 KV heads, head_dim 64, 40 keys."""
+    rng = np.random.default_rng(31)
+    q = rng.standard_normal((8, 64), dtype=np.float32)
+    k = rng.standard_normal((40, 2, 64), dtype=np.float32)
+    v = rng.standard_normal((40, 2, 64), dtype=np.float32)
+    return dict(q=q, k=k, v=v, sha256=_digest(q, k, v))
+
+
+def qwen35_prefill():
+    """Qwen35 prefill: 9 tokens after a 6-token prefix, 4 q / 2 KV heads, 64."""
+    rng = np.random.default_rng(32)
+    q = rng.standard_normal((9, 4, 64), dtype=np.float32)
+    k = rng.standard_normal((15, 2, 64), dtype=np.float32)
+    v = rng.standard_normal((15, 2, 64), dtype=np.float32)
+    return dict(q=q, k=k, v=v, prefix=6, sha256=_digest(q, k, v))
+
+
+def imrope_case():
+    """IMROPE on 3 tokens x 3 heads of head_dim 128 with sections
+    (11, 11, 10, 0) (64 rotary dims, 64 pass-through), base 1e7; text
+    positions [p, p, p, 0] and one multimodal lane set."""
+    rng = np.random.default_rng(33)
+    x = rng.standard_normal((3, 3, 128), dtype=np.float32)
+    lanes = np.array([[0, 0, 0, 0], [17, 17, 17, 0], [5, 9, 3, 0]], np.int32)
+    return dict(x=x, lanes=lanes, sections=(11, 11, 10, 0), base=10000000.0,
+                sha256=_digest(x, lanes))
+
+
+def gqa_step_case():
+    """qwen35_ops.causal_gqa_step: 4 q / 2 KV heads, dim 16, 7 keys."""
+    rng = np.random.default_rng(34)
+    q = rng.standard_normal((4, 16))
+    k = rng.standard_normal((7, 2, 16))
+    v = rng.standard_normal((7, 2, 16))
+    return dict(q=q, k=k, v=v, sha256=_digest(q, k, v))

@@ -1,0 +1,118 @@
+"""Generate golden vectors by running the REFERENCE (alpaccaroo) itself.
+
+Run in a container that has the reference checked out (default path below,
+or ALPACCAROO_REF=<dir containing the alpaccaroo package>):
+
+    python tests/golden/make_golden.py
+
+Inputs are regenerated from their seeds by tests/golden/cases.py (NumPy's
+PCG64 default_rng is stable across versions); each .npz stores the
+reference's outputs plus a SHA-256 of the input bytes, so a test can prove
+it rebuilt exactly the inputs the reference saw.  The reference runs its
+pure NumPy path here (its Numba kernels are disabled because the installed
+numba differs from its pin), which is the path the oracle restates.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+from tests.golden import cases  # noqa: E402
+
+REF = os.environ.get("ALPACCAROO_REF", "/root/reference")
+
+
+def _import_reference():
+    sys.path.insert(0, REF)
+    from alpaccaroo import model, qwen35_kernels, qwen35_ops  # noqa: WPS433
+    return model, qwen35_kernels, qwen35_ops
+
+
+def _llama_model(model_mod, n_ctx, n_head, n_kv, head_dim, n_rot, base, style):
+    hp = model_mod.Hyperparams(
+        arch="llama", n_layer=1, n_embd=n_head * head_dim, n_head=n_head, n_kv=n_kv,
+        n_ff=4 * n_head * head_dim, n_vocab=32, n_ctx_train=max(n_ctx, 4096),
+        head_dim=head_dim, n_rot=n_rot, rms_eps=1e-5, rope_base=base, rope_style=style)
+    m = model_mod.Model(hp, None)
+    m.n_ctx = n_ctx
+    m._init_cache()
+    return m
+
+
+def make_decode_config1(model_mod):
+    c = cases.decode_config1()
+    m = _llama_model(model_mod, c["L"], c["H"], c["KV"], c["D"], c["D"], c["base"], "norm")
+    K = np.empty_like(c["k_raw"])
+    for p in range(c["L"]):
+        K[p] = m._rope_np(c["k_raw"][p].reshape(-1), c["KV"], p).reshape(c["KV"], c["D"])
+    q = m._rope_np(c["q_raw"].reshape(-1), c["H"], c["L"] - 1)
+    out = m._attention_np(q, K, c["v"], c["H"] // c["KV"], 1.0 / np.sqrt(c["D"]))
+    rows = np.array(cases.CONFIG1_SAMPLE_ROWS)
+    np.savez_compressed(
+        os.path.join(HERE, "decode_config1.npz"), input_sha256=c["sha256"], q_rot=q,
+        k_rot_rows=K[rows], sample_rows=rows, out=out, cos_tab=m._rope_cos[rows],
+        sin_tab=m._rope_sin[rows])
+
+
+def make_rope_neox(model_mod):
+    c = cases.rope_neox()
+    m = _llama_model(model_mod, c["n_ctx"], c["H"], c["KV"], c["D"], c["n_rot"], c["base"], "neox")
+    single = np.stack([m._rope_np(c["q"][i].reshape(-1), c["H"], int(p))
+                       for i, p in enumerate(c["positions"])])
+    batch = m._rope_batch_np(c["k"].reshape(len(c["positions"]), -1), c["KV"], c["positions"])
+    np.savez_compressed(os.path.join(HERE, "rope_neox.npz"), input_sha256=c["sha256"],
+                        q_rot=single, k_rot=batch, cos_tab=m._rope_cos, sin_tab=m._rope_sin)
+
+
+def make_prefill(model_mod):
+    c = cases.prefill_small()
+    m = _llama_model(model_mod, c["t_kv"], c["H"], c["KV"], c["D"], c["D"], 10000.0, "norm")
+    out = m._attention_batch_np(c["q"], c["k"], c["v"], c["positions"], c["H"] // c["KV"],
+                                1.0 / np.sqrt(c["D"]))
+    w = cases.prefill_window()
+    m = _llama_model(model_mod, 64, w["H"], w["KV"], w["D"], w["D"], 10000.0, "norm")
+    outw = m._attention_batch_window_np(w["q"], w["k"], w["v"], w["positions"],
+                                        w["H"] // w["KV"], 1.0 / np.sqrt(w["D"]),
+                                        w["window"], w["kv_start"])
+    np.savez_compressed(os.path.join(HERE, "prefill_small.npz"), input_sha256=c["sha256"],
+                        out=out, window_input_sha256=w["sha256"], out_window=outw)
+
+
+def make_qwen35(qk_mod, ops_mod):
+    c = cases.qwen35_decode()
+    out = qk_mod.qwen35_full_attention_decode(c["q"], c["k"], c["v"])
+    p = cases.qwen35_prefill()
+    outp = qk_mod.qwen35_full_attention_prefill(p["q"], p["k"], p["v"], p["prefix"])
+    r = cases.imrope_case()
+    rot = np.array([[ops_mod.imrope_rotate(list(map(float, r["x"][i, h])),
+                                           [int(x) for x in r["lanes"][i]], r["sections"],
+                                           frequency_base=r["base"])
+                     for h in range(r["x"].shape[1])] for i in range(r["x"].shape[0])])
+    lanes = np.array([ops_mod.imrope_lane_for_pair(j, r["sections"])
+                      for j in range(sum(r["sections"]))])
+    g = cases.gqa_step_case()
+    gqa = np.array(ops_mod.causal_gqa_step(g["q"].tolist(), g["k"].tolist(), g["v"].tolist()))
+    np.savez_compressed(os.path.join(HERE, "qwen35.npz"), decode_sha256=c["sha256"],
+                        decode_out=out, prefill_sha256=p["sha256"], prefill_out=outp,
+                        imrope_sha256=r["sha256"], imrope_out=rot, imrope_lanes=lanes,
+                        gqa_sha256=g["sha256"], gqa_out=gqa)
+
+
+def main():
+    model_mod, qk_mod, ops_mod = _import_reference()
+    make_decode_config1(model_mod)
+    make_rope_neox(model_mod)
+    make_prefill(model_mod)
+    make_qwen35(qk_mod, ops_mod)
+    for f in sorted(os.listdir(HERE)):
+        if f.endswith(".npz"):
+            print(f, os.path.getsize(os.path.join(HERE, f)))
+
+
+if __name__ == "__main__":
+    main()

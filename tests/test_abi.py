@@ -1,0 +1,119 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol
+include/b2attn.h declares, and rejects bad arguments on the host with the
+documented status codes (these returns happen before any CUDA call)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from alpacca_open_sourced_by_jt_b200 import _lib, build
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                      "b2attn.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _lib.load()
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(b2a_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_bound_symbols():
+    assert declared_symbols() == sorted(n for n, _, _ in _lib.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_version(lib):
+    assert lib.b2a_version() == 1
+
+
+def test_workspace_and_split_helpers(lib):
+    sr = lib.b2a_decode_split_rows(16, 8, 32768, _lib.BF16)
+    assert sr % 64 == 0 and 256 <= sr <= 2048
+    n_split = -(-32768 // sr)
+    ws = lib.b2a_decode_workspace_bytes(16, 32, 128, 32768, sr)
+    assert ws >= 16 * 32 * n_split * (128 + 2) * 4
+    assert lib.b2a_decode_workspace_bytes(0, 32, 128, 1, 64) == 0
+
+
+def _decode(lib, **kw):
+    args = dict(q=1 << 20, k=1 << 20, v=1 << 20, lens=1 << 20, out=1 << 20, lse=None,
+                ws=1 << 20, ws_bytes=1 << 30, B=1, H=32, KV=8, D=128, n_ctx=1024, seq_stride=0,
+                dt=_lib.BF16, scale=0.088, max_len=1024, split=0, stream=None)
+    args.update(kw)
+    return lib.b2a_decode(*args.values())
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(q=None), _lib.ERR_ARG),
+    (dict(B=0), _lib.ERR_ARG),
+    (dict(H=30), _lib.ERR_SHAPE),
+    (dict(H=8 * 17), _lib.ERR_UNSUPPORTED),
+    (dict(max_len=2048), _lib.ERR_SHAPE),
+    (dict(dt=7), _lib.ERR_DTYPE),
+    (dict(scale=-1.0), _lib.ERR_ARG),
+    (dict(split=100), _lib.ERR_ARG),
+    (dict(ws_bytes=16), _lib.ERR_WORKSPACE),
+    (dict(B=2, seq_stride=5), _lib.ERR_SHAPE),
+    (dict(q=(1 << 20) + 4), _lib.ERR_ALIGN),
+    (dict(D=96), _lib.ERR_UNSUPPORTED),
+])
+def test_decode_rejects_bad_arguments(lib, kw, code):
+    assert _decode(lib, **kw) == code
+    assert _lib.last_error()
+
+
+def test_prefill_rejects_bad_arguments(lib):
+    p = 1 << 20
+    assert lib.b2a_prefill(None, p, p, p, p, 8, 8, 4, 2, 64, _lib.BF16, _lib.F32, 0.1, 0, 0,
+                           None) == _lib.ERR_ARG
+    assert lib.b2a_prefill(p, p, p, p, p, 8, 8, 5, 2, 64, _lib.BF16, _lib.F32, 0.1, 0, 0,
+                           None) == _lib.ERR_SHAPE
+    assert lib.b2a_prefill(p, p, p, p, p, 8, 8, 4, 2, 64, _lib.F32, _lib.F32, 0.1, 0, 0,
+                           None) == _lib.ERR_DTYPE
+    assert lib.b2a_prefill(p, p, p, p, p, 8, 8, 4, 2, 96, _lib.BF16, _lib.F32, 0.1, 0, 0,
+                           None) == _lib.ERR_UNSUPPORTED
+    assert lib.b2a_prefill(p + 2, p, p, p, p, 8, 8, 4, 2, 64, _lib.BF16, _lib.F32, 0.1, 0, 0,
+                           None) == _lib.ERR_ALIGN
+    # zero query tokens is a successful no-op
+    assert lib.b2a_prefill(p, p, p, p, p, 0, 8, 4, 2, 64, _lib.BF16, _lib.F32, 0.1, 0, 0,
+                           None) == _lib.OK
+
+
+def test_rope_rejects_bad_arguments(lib):
+    p = 1 << 20
+    # n_tok = 0: every argument check runs, then the call returns before any launch
+    base = [p, 0, p, 0, p, 0, None, None, None, p, p, 16, p, 0, p, p, 0, 16, _lib.F32, None,
+            _lib.F32, 0, 2, 1, 64, 64, _lib.ROPE_NORM, None]
+    assert lib.b2a_rope_append(*base) == _lib.OK
+    bad = list(base)
+    bad[25] = 63  # odd n_rot
+    assert lib.b2a_rope_append(*bad) == _lib.ERR_SHAPE
+    bad = list(base)
+    bad[26] = 9  # style
+    assert lib.b2a_rope_append(*bad) == _lib.ERR_ARG
+    bad = list(base)
+    bad[13] = 2  # tok_seq_mode
+    assert lib.b2a_rope_append(*bad) == _lib.ERR_ARG
+    sec = (ctypes.c_int * 4)(0, 0, 0, 0)
+    assert lib.b2a_imrope_append(p, 0, p, 0, p, 0, p, sec, 1e4, 1.0, p, 0, p, p, 0, 16, _lib.F32,
+                                 p, _lib.F32, 1, 2, 1, 64, None) == _lib.ERR_ARG
+    sec = (ctypes.c_int * 4)(40, 0, 0, 0)
+    assert lib.b2a_imrope_append(p, 0, p, 0, p, 0, p, sec, 1e4, 1.0, p, 0, p, p, 0, 16, _lib.F32,
+                                 p, _lib.F32, 1, 2, 1, 64, None) == _lib.ERR_SHAPE
+
+
+def test_lse_combine_rejects_bad_arguments(lib):
+    assert lib.b2a_lse_combine(None, 1, 2, 3, 4, 5, None, None) == _lib.ERR_ARG
+    assert lib.b2a_lse_combine(16, 16, 0, 3, 4, 16, None, None) == _lib.ERR_ARG

@@ -1,0 +1,126 @@
+"""tcgen05 causal prefill vs the oracle (the reference's NumPy einsum path).
+
+The kernel takes 16-bit q/K/V and accumulates in fp32 (P is rounded to 16
+bits for the second MMA).  The oracle runs in fp32 on the same 16-bit
+inputs; the bar is 2e-2 max abs error on unit-variance outputs.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests.conftest import max_abs_err, rel_err
+from tests.golden import cases
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(T, t_kv, H, KV, D, dt, dev, positions=None, window=0, kv_start=0, out_dtype=None,
+         seed=0):
+    from alpacca_open_sourced_by_jt_b200 import device
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn((T, H, D), generator=g).to(dt)
+    k = torch.randn((t_kv, KV, D), generator=g).to(dt)
+    v = torch.randn((t_kv, KV, D), generator=g).to(dt)
+    if positions is None:
+        positions = np.arange(kv_start + t_kv - T, kv_start + t_kv, dtype=np.int32)
+    pos = torch.from_numpy(np.asarray(positions, np.int32))
+    out = device.prefill(q.to(dev), k.to(dev), v.to(dev), pos.to(dev), window=window,
+                         kv_start=kv_start, out_dtype=out_dtype or torch.float32)
+    torch.cuda.synchronize()
+    ref = oracle.attention_batch(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                 np.asarray(positions, np.int32), H // KV, 1 / math.sqrt(D),
+                                 window, kv_start)
+    return out.float().cpu().numpy().reshape(T, -1), ref
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("T", [1, 77, 128, 300])
+def test_causal_from_zero(cuda_dev, dt, D, T):
+    out, ref = _run(T, T, 8, 2, D, dt, cuda_dev, seed=T)
+    assert max_abs_err(out, ref) < 2e-2
+
+
+@pytest.mark.parametrize("group", [1, 4, 8])
+def test_gqa_groups_with_prefix(cuda_dev, group):
+    # a 200-token chunk after a 333-token prefix: 533 keys, queries at 333..532
+    out, ref = _run(200, 533, 2 * group, 2, 128, torch.bfloat16, cuda_dev, seed=group)
+    assert max_abs_err(out, ref) < 2e-2
+
+
+def test_window_and_kv_start(cuda_dev):
+    out, ref = _run(150, 260, 8, 2, 64, torch.bfloat16, cuda_dev,
+                    positions=np.arange(200, 350, dtype=np.int32), window=64, kv_start=100)
+    assert max_abs_err(out, ref) < 2e-2
+
+
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16])
+def test_16bit_output(cuda_dev, out_dtype):
+    out, ref = _run(256, 256, 4, 1, 128, torch.bfloat16, cuda_dev, out_dtype=out_dtype)
+    assert max_abs_err(out, ref) < 2e-2
+
+
+def test_config2_shape(cuda_dev):
+    """BASELINE config 2 geometry (S=2048, 32/8 heads, D=128, bf16, bf16 out)
+    against the oracle on a subset of heads' rows (the oracle's fp32 einsum
+    over all 32 heads x 2048^2 scores is too slow for a unit test)."""
+    from alpacca_open_sourced_by_jt_b200 import device
+    S, H, KV, D = 2048, 32, 8, 128
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn((S, H, D), generator=g).to(torch.bfloat16)
+    k = torch.randn((S, KV, D), generator=g).to(torch.bfloat16)
+    v = torch.randn((S, KV, D), generator=g).to(torch.bfloat16)
+    pos = torch.arange(S, dtype=torch.int32)
+    out = device.prefill(q.to(cuda_dev), k.to(cuda_dev), v.to(cuda_dev), pos.to(cuda_dev))
+    out = out.float().cpu().numpy()
+    rows = np.r_[0:3, 127:130, 1000:1003, 2040:2048]
+    kvh = 3
+    ref = oracle.attention_batch(q[rows][:, kvh * 4:(kvh + 1) * 4].float().numpy(),
+                                 k[:, kvh:kvh + 1].float().numpy(), v[:, kvh:kvh + 1].float().numpy(),
+                                 rows.astype(np.int32), 4, 1 / math.sqrt(D))
+    got = out[rows][:, kvh * 4:(kvh + 1) * 4].reshape(len(rows), -1)
+    assert max_abs_err(got, ref) < 2e-2
+
+
+def test_determinism(cuda_dev):
+    from alpacca_open_sourced_by_jt_b200 import device
+    q = torch.randn((384, 8, 128), device=cuda_dev, dtype=torch.bfloat16)
+    k = torch.randn((384, 2, 128), device=cuda_dev, dtype=torch.bfloat16)
+    v = torch.randn((384, 2, 128), device=cuda_dev, dtype=torch.bfloat16)
+    pos = torch.arange(384, dtype=torch.int32, device=cuda_dev)
+    a = device.prefill(q, k, v, pos)
+    b = device.prefill(q, k, v, pos)
+    assert torch.equal(a, b)
+
+
+def test_golden_through_attention_batch_dropin(cuda_dev, golden):
+    """The reference's cuda.attention_batch signature on the reference's own
+    golden case (fp32 host inputs, rounded to fp16 for the tensor cores)."""
+    from alpacca_open_sourced_by_jt_b200 import cuda
+    g = golden("prefill_small.npz")
+    c = cases.prefill_small()
+    out = cuda.attention_batch(c["q"], c["k"], c["v"], c["positions"], c["H"] // c["KV"],
+                               1 / math.sqrt(c["D"]))
+    assert out.shape == g["out"].shape
+    assert max_abs_err(out, g["out"]) < 5e-3
+    w = cases.prefill_window()
+    outw = cuda.attention_batch(w["q"], w["k"], w["v"], w["positions"], w["H"] // w["KV"],
+                                1 / math.sqrt(w["D"]), w["window"], w["kv_start"])
+    assert max_abs_err(outw, g["out_window"]) < 5e-3
+    # unsupported geometry is declined like the reference (None), not faked
+    assert cuda.attention_batch(np.zeros((2, 2, 256), np.float32), np.zeros((2, 1, 256), np.float32),
+                                np.zeros((2, 1, 256), np.float32), np.array([0, 1], np.int32), 2,
+                                0.0625) is None
+
+
+def test_qwen35_dropins(cuda_dev, golden):
+    from alpacca_open_sourced_by_jt_b200 import qwen35_kernels as q35
+    g = golden("qwen35.npz")
+    c = cases.qwen35_decode()
+    assert rel_err(q35.qwen35_full_attention_decode(c["q"], c["k"], c["v"]), g["decode_out"]) < 1e-4
+    p = cases.qwen35_prefill()
+    out = q35.qwen35_full_attention_prefill(p["q"], p["k"], p["v"], p["prefix"])
+    assert max_abs_err(out, g["prefill_out"]) < 5e-3
