@@ -156,6 +156,7 @@ def bench_decode(dev, rank, steps, warmup, dist):
     import torch
     from alpacca_open_sourced_by_jt_b200 import device
     B, L, H, KV, D = WL["B"], WL["L"], WL["H"], WL["KV"], WL["D"]
+    log(f"decode workload B={B} L={L} H={H} KV={KV} D={D}")
     g = torch.Generator(device=dev).manual_seed(4 + rank)
     kc = torch.randn((B, L, KV, D), device=dev, dtype=torch.bfloat16, generator=g)
     vc = torch.randn((B, L, KV, D), device=dev, dtype=torch.bfloat16, generator=g)
@@ -342,9 +343,13 @@ def run_ours(args):
     achieved = per_step / (ms / args.steps * 1e-3) / 1e9   # per rank, per launch pair
     result = None
     if rank == 0:
-        e2e = bench_e2e(dev, st, args.steps, args.warmup)
-        e2e["value"] *= world
-        pf = bench_prefill(dev, args.steps, args.warmup) if not args.no_prefill else None
+        e2e = None
+        if args.only in (None, "e2e"):
+            e2e = bench_e2e(dev, st, args.steps, args.warmup)
+            e2e["value"] *= world
+        pf = None
+        if args.only in (None, "prefill") and not args.no_prefill:
+            pf = bench_prefill(dev, args.steps, args.warmup)
         _lib.raise_device_error()
         cpu = cpu_decode_baseline(st) if (world == 1 and not args.no_cpu_baseline) else None
         traffic = profiled_traffic("decode_mma_kernel bf16 D128 NT1")
@@ -366,8 +371,9 @@ def run_ours(args):
                          "kernel": "decode_mma_kernel<bf16,128,1> + decode_combine_kernel, "
                                    "timed together per b2a_decode call"},
             "gpu_launches": 2 * args.steps,
-            "e2e": e2e,
         }
+        if e2e:
+            result["e2e"] = e2e
         if cpu:
             result["cpu_baseline"] = cpu
         if clk:
@@ -448,7 +454,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--only", choices=["decode", "e2e", "prefill"], default=None,
+                    help="profiling aid: run the decode timing plus only this extra part")
+    ap.add_argument("--batch", type=int, default=WL["B"],
+                    help="profiling aid: sequences per GPU (default 16)")
+    ap.add_argument("--ctx", type=int, default=WL["L"],
+                    help="profiling aid: cached tokens per sequence (default 32768)")
     args = ap.parse_args()
+    WL["B"], WL["L"] = args.batch, args.ctx
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
