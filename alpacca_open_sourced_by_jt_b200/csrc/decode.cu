@@ -728,3 +728,67 @@ int b2a_lse_combine(const float* o_parts, const float* lse_parts, int G, int row
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// Decode for callers that cannot allocate device memory
+// ===========================================================================
+// Some callers of this library can't call cudaMalloc. A serving process may
+// have reserved nearly all of HBM for its KV cache, or may run behind an
+// allocator that owns every device buffer. An embedding host across an FFI
+// may have no device allocator at all. For them, b2a_decode_noalloc keeps
+// the split partials in this fixed file-scope array instead of a
+// caller-supplied workspace. Every GPU that loads the library holds the
+// array until the process exits.
+#include <mutex>
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = B2A_DECODE_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
+
+std::mutex g_scratch_mu;
+void* g_scratch_addr[64] = {};  // device address of g_decode_scratch, per device
+
+// Device address of the scratch array on the current device. The host-side
+// name g_decode_scratch is only a stand-in, so the address is looked up once
+// per device with that device current.
+int scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return b2a_host::cuda_fail(e, "decode_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(B2A_ERR_UNSUPPORTED, "decode_noalloc: device %d >= 64", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess || !p) return b2a_host::cuda_fail(e, "decode_noalloc: cudaGetSymbolAddress");
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return B2A_OK;
+}
+
+}  // namespace
+
+extern "C" int b2a_decode_noalloc(const float* q, const void* k_cache, const void* v_cache,
+                                  const int* lens_dev, float* out, float* lse_out, int B, int H,
+                                  int KV, int D, int n_ctx, long long seq_stride, int kv_dtype,
+                                  float scale, int max_len, int split_rows, void* stream) {
+  if (B <= 0 || H <= 0 || KV <= 0 || D <= 0 || max_len < 0)
+    return fail(B2A_ERR_ARG, "decode_noalloc: sizes must be positive");
+  if (split_rows <= 0) split_rows = b2a_decode_split_rows(B, KV, max_len, kv_dtype);
+  const size_t need = b2a_decode_workspace_bytes(B, H, D, max_len, split_rows);
+  if (need > kNoAllocScratchBytes)
+    return fail(B2A_ERR_WORKSPACE,
+                "decode_noalloc: B=%d H=%d D=%d max_len=%d split_rows=%d needs %zu bytes of "
+                "scratch but the static array holds %zu; raise split_rows or call b2a_decode "
+                "with a caller workspace",
+                B, H, D, max_len, split_rows, need, kNoAllocScratchBytes);
+  void* ws = nullptr;
+  const int rc = scratch_address(&ws);
+  if (rc) return rc;
+  // The partials need no clearing: each CTA writes every partial the combine
+  // kernel later reads for this call.
+  return b2a_decode(q, k_cache, v_cache, lens_dev, out, lse_out, ws, kNoAllocScratchBytes, B, H,
+                    KV, D, n_ctx, seq_stride, kv_dtype, scale, max_len, split_rows, stream);
+}

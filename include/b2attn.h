@@ -98,6 +98,27 @@ int b2a_decode(const float* q, const void* k_cache, const void* v_cache, const i
                int KV, int D, int n_ctx, long long seq_stride, int kv_dtype, float scale,
                int max_len, int split_rows, void* stream);
 
+/* Decode without any device allocation. This entry point has no counterpart
+ * in the reference.  It is for callers that can't call cudaMalloc: a serving
+ * process that reserved nearly all of HBM for its KV cache up front, a host
+ * whose allocator owns every device buffer, or an FFI host with no device
+ * allocator.  Same arguments and results as b2a_decode, minus the workspace:
+ * the split partials live in one static device array of
+ * B2A_DECODE_NOALLOC_SCRATCH_BYTES (16 MiB), which every GPU that loads the
+ * library holds until the process exits.
+ *   - A call whose partials (b2a_decode_workspace_bytes) exceed the array is
+ *     rejected with B2A_ERR_WORKSPACE; a larger split_rows needs less.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - All calls share the array and it keeps the last call's contents: calls
+ *     that overlap on the GPU (two streams, or two threads without ordering)
+ *     race on it.  Nothing in it needs to start at zero. */
+#define B2A_DECODE_NOALLOC_SCRATCH_BYTES (16u << 20)
+int b2a_decode_noalloc(const float* q, const void* k_cache, const void* v_cache,
+                       const int* lens_dev, float* out, float* lse_out, int B, int H, int KV,
+                       int D, int n_ctx, long long seq_stride, int kv_dtype, float scale,
+                       int max_len, int split_rows, void* stream);
+
 /* Merge G partial decodes of the same queries over disjoint KV ranges (the
  * long-context shard combine).  Same algebra as _attention_decode_combine
  * (alpaccaroo/cuda.py:674-694) with normalised parts:
