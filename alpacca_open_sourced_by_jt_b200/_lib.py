@@ -56,8 +56,8 @@ SIGNATURES = [
     ("b2a_decode_noalloc", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                    c_int, c_int, c_int, c_int, c_int, c_longlong, c_int,
                                    c_float, c_int, c_int, c_void_p]),
-    ("b2a_lse_combine", c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
-                                c_void_p]),
+    ("b2a_lse_combine", c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_int, c_int, c_int,
+                                c_void_p, c_void_p, c_void_p]),
     ("b2a_prefill", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
                             c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_int, c_void_p]),
     ("b2a_rope_append", c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_void_p,

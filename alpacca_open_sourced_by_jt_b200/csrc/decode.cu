@@ -480,21 +480,22 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(
 // ---------------------------------------------------------------------------
 // Cross-shard log-sum-exp combine (normalised parts, natural-log lse)
 // ---------------------------------------------------------------------------
-__global__ void lse_combine_kernel(const float* __restrict__ o_parts,
-                                   const float* __restrict__ lse_parts, int G, int rows, int D,
-                                   float* __restrict__ out, float* __restrict__ lse_out) {
+__global__ void lse_combine_kernel(const float* __restrict__ o_parts, long long o_stride,
+                                   const float* __restrict__ lse_parts, long long lse_stride,
+                                   int G, int rows, int D, float* __restrict__ out,
+                                   float* __restrict__ lse_out) {
   const int r = blockIdx.x;
   float M = -INFINITY;
-  for (int g = 0; g < G; ++g) M = fmaxf(M, lse_parts[static_cast<size_t>(g) * rows + r]);
+  for (int g = 0; g < G; ++g) M = fmaxf(M, lse_parts[g * lse_stride + r]);
   const float Mref = (M == -INFINITY) ? 0.f : M;
   float L = 0.f;
-  for (int g = 0; g < G; ++g) L += expf(lse_parts[static_cast<size_t>(g) * rows + r] - Mref);
+  for (int g = 0; g < G; ++g) L += expf(lse_parts[g * lse_stride + r] - Mref);
   const float invL = (L > 0.f) ? 1.f / L : 0.f;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float acc = 0.f;
     for (int g = 0; g < G; ++g) {
-      const float w = expf(lse_parts[static_cast<size_t>(g) * rows + r] - Mref);
-      acc += w * o_parts[(static_cast<size_t>(g) * rows + r) * D + d];
+      const float w = expf(lse_parts[g * lse_stride + r] - Mref);
+      acc += w * o_parts[g * o_stride + static_cast<size_t>(r) * D + d];
     }
     out[static_cast<size_t>(r) * D + d] = acc * invL;
   }
@@ -716,12 +717,17 @@ int b2a_decode(const float* q, const void* k_cache, const void* v_cache, const i
   return B2A_OK;
 }
 
-int b2a_lse_combine(const float* o_parts, const float* lse_parts, int G, int rows, int D,
-                    float* out, float* lse_out, void* stream) {
+int b2a_lse_combine(const float* o_parts, long long o_part_stride, const float* lse_parts,
+                    long long lse_part_stride, int G, int rows, int D, float* out,
+                    float* lse_out, void* stream) {
   if (!o_parts || !lse_parts || !out) return fail(B2A_ERR_ARG, "lse_combine: null pointer argument");
   if (G <= 0 || rows <= 0 || D <= 0) return fail(B2A_ERR_ARG, "lse_combine: sizes must be positive");
-  lse_combine_kernel<<<rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(o_parts, lse_parts, G,
-                                                                        rows, D, out, lse_out);
+  if (o_part_stride == 0) o_part_stride = static_cast<long long>(rows) * D;
+  if (lse_part_stride == 0) lse_part_stride = rows;
+  if (o_part_stride < static_cast<long long>(rows) * D || lse_part_stride < rows)
+    return fail(B2A_ERR_SHAPE, "lse_combine: part strides overlap the parts");
+  lse_combine_kernel<<<rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      o_parts, o_part_stride, lse_parts, lse_part_stride, G, rows, D, out, lse_out);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "lse_combine launch");
   return B2A_OK;

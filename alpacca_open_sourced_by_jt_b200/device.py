@@ -113,15 +113,21 @@ def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, lens: 
 
 def lse_combine(o_parts: torch.Tensor, lse_parts: torch.Tensor, *, out=None, lse=None,
                 stream=None) -> torch.Tensor:
-    """Merge G normalised partial outputs (G, R, D) by their lse (G, R)."""
-    _cuda_contig("o_parts", o_parts)
-    _cuda_contig("lse_parts", lse_parts)
+    """Merge G normalised partial outputs (G, R, D) by their lse (G, R).
+
+    Each part must be contiguous ((R, D) and (R,)); the parts may sit at any
+    stride from one another (e.g. views into one gathered buffer)."""
     G, R, D = o_parts.shape
     _need(lse_parts.shape == (G, R), "lse_parts must be (G, R)")
+    _need(o_parts.is_cuda and lse_parts.is_cuda, "parts must be CUDA tensors")
+    _need(o_parts.stride(2) == 1 and o_parts.stride(1) == D and lse_parts.stride(1) == 1,
+          "each part must be contiguous")
+    _need(o_parts.dtype == lse_parts.dtype == torch.float32, "parts must be f32")
     if out is None:
         out = torch.empty((R, D), dtype=torch.float32, device=o_parts.device)
-    _lib.check(_lib.load().b2a_lse_combine(_ptr(o_parts), _ptr(lse_parts), G, R, D, _ptr(out),
-                                           _ptr(lse), _stream(stream)))
+    _lib.check(_lib.load().b2a_lse_combine(_ptr(o_parts), o_parts.stride(0), _ptr(lse_parts),
+                                           lse_parts.stride(0), G, R, D, _ptr(out), _ptr(lse),
+                                           _stream(stream)))
     return out
 
 

@@ -45,6 +45,7 @@ sys.path.insert(0, REPO)
 METRIC = "decode-attn KV GB/s (% HBM peak) @32K ctx; prefill-attn TFLOPS; at 1/2/4/8 GPU"
 WL = dict(B=16, L=32768, H=32, KV=8, D=128)            # decode workload (per rank)
 PF = dict(S=2048, H=32, KV=8, D=128)                   # prefill workload (config 2)
+LC = dict(B=4, L=131072, H=64, KV=8, D=128)            # long-context split (config 4)
 FALLBACK_HBM = 6650.0
 FALLBACK_BF16 = 1590.0
 SPEC_HBM = 8000.0
@@ -186,6 +187,56 @@ def bench_decode(dev, rank, steps, warmup, dist):
         dist.barrier()
     torch.cuda.synchronize()
     return dict(ms=ms, split=split, kc=kc, vc=vc, q=q, lens=lens, ws=ws, out=out)
+
+
+def bench_longctx(dev, rank, world, steps, warmup, dist):
+    """4 sequences x 131072 rows, 64 q / 8 KV heads, D=128,
+    bf16; the KV rows of every sequence are split across the ranks, each rank
+    decodes its rows, one NCCL all-gather moves the (o, lse) parts and the
+    LSE-combine kernel merges them.  Total work is fixed (strong scaling)."""
+    import torch
+    from alpacca_open_sourced_by_jt_b200.longctx import LongContextDecoder, shard_rows
+    B, L, H, KV, D = LC["B"], LC["L"], LC["H"], LC["KV"], LC["D"]
+    a, b = shard_rows(L, rank, world)
+    n = b - a
+    g = torch.Generator(device=dev).manual_seed(3 + rank)
+    ks = torch.randn((B, n, KV, D), device=dev, dtype=torch.bfloat16, generator=g)
+    vs = torch.randn((B, n, KV, D), device=dev, dtype=torch.bfloat16, generator=g)
+    gq = torch.Generator(device=dev).manual_seed(3)
+    q = torch.randn((B, H, D), device=dev, dtype=torch.float32, generator=gq)
+    lens = torch.full((B,), n, dtype=torch.int32, device=dev)
+    dec = LongContextDecoder()
+
+    def step():
+        dec.decode(q, ks, vs, lens, max_len=n)
+
+    for _ in range(max(warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    nsteps = max(10, min(steps, 500))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(nsteps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del ks, vs
+    per_step = decode_bytes(B, L, KV, D)
+    return {"metric": "long-context split decode KV GB/s (config 4)",
+            "value": round(per_step / (ms / nsteps * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "ms_per_step": round(ms / nsteps, 4), "steps": nsteps, "n_gpus": world,
+            "scaling": "strong",
+            "config": "4 seqs x 131072 rows (split over the GPUs), 64 q / 8 KV heads, D=128, "
+                      "bf16; per step: decode of local rows with lse, one NCCL all-gather of "
+                      "B*H*(D+1) f32 per rank, LSE-combine kernel"}
 
 
 def bench_e2e(dev, st, steps, warmup):
@@ -331,6 +382,9 @@ def run_ours(args):
         clocks.start()
     st = bench_decode(dev, rank, args.steps, args.warmup, dist)
     clk = clocks.stop() if clocks else None
+    lc = None
+    if args.only in (None, "longctx"):
+        lc = bench_longctx(dev, rank, world, args.steps, args.warmup, dist)
     ms = st["ms"]
     if dist is not None:
         t = torch.tensor([ms], device=dev)
@@ -374,6 +428,8 @@ def run_ours(args):
         }
         if e2e:
             result["e2e"] = e2e
+        if lc:
+            result["longctx"] = lc
         if cpu:
             result["cpu_baseline"] = cpu
         if clk:
@@ -454,7 +510,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
-    ap.add_argument("--only", choices=["decode", "e2e", "prefill"], default=None,
+    ap.add_argument("--only", choices=["decode", "e2e", "prefill", "longctx"], default=None,
                     help="profiling aid: run the decode timing plus only this extra part")
     ap.add_argument("--batch", type=int, default=WL["B"],
                     help="profiling aid: sequences per GPU (default 16)")

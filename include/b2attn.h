@@ -123,9 +123,13 @@ int b2a_decode_noalloc(const float* q, const void* k_cache, const void* v_cache,
  * long-context shard combine).  Same algebra as _attention_decode_combine
  * (alpaccaroo/cuda.py:674-694) with normalised parts:
  *   out[r] = sum_g exp(lse[g][r] - L) * o[g][r],  L = log sum_g exp(lse[g][r])
- *   o_parts f32 [G][rows][D], lse_parts f32 [G][rows]; lse_out may be NULL. */
-int b2a_lse_combine(const float* o_parts, const float* lse_parts, int G, int rows, int D,
-                    float* out, float* lse_out, void* stream);
+ * Part g's o rows start at o_parts + g*o_part_stride ([rows][D] f32) and its
+ * lse at lse_parts + g*lse_part_stride ([rows] f32); a stride of 0 means
+ * dense ([G][rows][D], [G][rows]), so one gathered buffer holding each rank's
+ * o followed by its lse can be read in place.  lse_out may be NULL. */
+int b2a_lse_combine(const float* o_parts, long long o_part_stride, const float* lse_parts,
+                    long long lse_part_stride, int G, int rows, int D, float* out,
+                    float* lse_out, void* stream);
 
 /* ---- (2) causal prefill on tcgen05 --------------------------------------
  *

@@ -115,5 +115,6 @@ def test_rope_rejects_bad_arguments(lib):
 
 
 def test_lse_combine_rejects_bad_arguments(lib):
-    assert lib.b2a_lse_combine(None, 1, 2, 3, 4, 5, None, None) == _lib.ERR_ARG
-    assert lib.b2a_lse_combine(16, 16, 0, 3, 4, 16, None, None) == _lib.ERR_ARG
+    assert lib.b2a_lse_combine(None, 0, 16, 0, 2, 3, 4, 16, None, None) == _lib.ERR_ARG
+    assert lib.b2a_lse_combine(16, 0, 16, 0, 0, 3, 4, 16, None, None) == _lib.ERR_ARG
+    assert lib.b2a_lse_combine(16, 5, 16, 0, 2, 3, 4, 16, None, None) == _lib.ERR_SHAPE
