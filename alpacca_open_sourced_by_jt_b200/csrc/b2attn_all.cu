@@ -4,3 +4,4 @@
 #include "decode.cu"
 #include "rope_append.cu"
 #include "prefill.cu"
+#include "prefill_pair.cu"

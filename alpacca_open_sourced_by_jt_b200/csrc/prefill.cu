@@ -25,6 +25,8 @@
 
 #include <limits.h>
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include <type_traits>
 
@@ -358,13 +360,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(
       const int lo = (window > 0 && my_pos != INT_MIN)
                          ? static_cast<int>(max(static_cast<long long>(my_pos) - window + 1 - kv0, -1ll))
                          : -1;
-      float mx = -INFINITY;
+      // branch-free mask (a short-circuit test compiles to a branch per
+      // element); four partial maxima keep the FMNMX chain short
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) {
-        const float x = (c <= hi && c >= lo) ? s[c] * sscale : -INFINITY;
-        s[c] = x;
-        mx = fmaxf(mx, x);
+      for (int c = 0; c < kBN; c += 4) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int cc = c + e;
+          s[cc] = ((cc <= hi) & (cc >= lo)) ? s[cc] * sscale : -INFINITY;
+        }
+        mx0 = fmaxf(mx0, s[c]);
+        mx1 = fmaxf(mx1, s[c + 1]);
+        mx2 = fmaxf(mx2, s[c + 2]);
+        mx3 = fmaxf(mx3, s[c + 3]);
       }
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
       const float mnew = fmaxf(m, mx);
       const bool need = mnew > m + kRescaleThreshold;
       const bool warp_need = __any_sync(0xffffffffu, need);
@@ -374,13 +385,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(
         m = mnew;
       }
       const float mref = (m == -INFINITY) ? 0.f : m;
-      float sum = 0.f;
+      float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) {
-        const float p = fast_exp2(s[c] - mref);
-        s[c] = p;
-        sum += p;
+      for (int c = 0; c < kBN; c += 2) {
+        const float p0 = fast_exp2(s[c] - mref);
+        const float p1 = fast_exp2(s[c + 1] - mref);
+        s[c] = p0;
+        s[c + 1] = p1;
+        sum0 += p0;
+        sum1 += p1;
       }
+      const float sum = sum0 + sum1;
       l = l * alpha + sum;
 
       // P buffer and O are free once PV of the previous tile completed
@@ -459,6 +474,18 @@ using P::kBM;
 using P::prefill_kernel;
 using b2a_host::fail;
 
+// Defined in prefill_pair.cu (same translation unit).
+template <typename T, typename TO, int D>
+int launch_prefill_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                        const int* pos, void* out, int n_q, int t_kv, int H, int KV, float scale,
+                        int window, int kv_start, cudaStream_t st);
+
+// B2ATTN_PREFILL=single forces the one-tile kernel (for testing both paths).
+bool force_single_tile() {
+  const char* e = getenv("B2ATTN_PREFILL");
+  return e && strcmp(e, "single") == 0;
+}
+
 template <typename T, typename TO, int D>
 int launch_prefill(const void* q, const void* k, const void* v, const int* pos, void* out, int n_q,
                    int t_kv, int H, int KV, float scale, int window, int kv_start, cudaStream_t st) {
@@ -477,6 +504,9 @@ int launch_prefill(const void* q, const void* k, const void* v, const int* pos, 
   if (rc) return rc;
   rc = b2a_host::make_tmap(&tv, tdt, 3, const_cast<void*>(v), kdims, kstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
+  if ((H / KV) % 2 == 0 && !force_single_tile())
+    return launch_prefill_pair<T, TO, D>(tq, tk, tv, pos, out, n_q, t_kv, H, KV, scale, window,
+                                         kv_start, st);
   auto kern = prefill_kernel<T, TO, D>;
   // >= 116 KB keeps one CTA per SM, so the 512-column TMEM allocation never
   // waits on a co-resident CTA.

@@ -17,6 +17,17 @@ from tests.golden import cases
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(params=["pair", "single"])
+def kernel(request, monkeypatch):
+    """Run a test on both prefill kernels: the paired-head persistent kernel
+    (default for even GQA groups) and the one-tile kernel (odd groups)."""
+    if request.param == "single":
+        monkeypatch.setenv("B2ATTN_PREFILL", "single")
+    else:
+        monkeypatch.delenv("B2ATTN_PREFILL", raising=False)
+    return request.param
+
+
 def _run(T, t_kv, H, KV, D, dt, dev, positions=None, window=0, kv_start=0, out_dtype=None,
          seed=0):
     from alpacca_open_sourced_by_jt_b200 import device
@@ -39,31 +50,31 @@ def _run(T, t_kv, H, KV, D, dt, dev, positions=None, window=0, kv_start=0, out_d
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("T", [1, 77, 128, 300])
-def test_causal_from_zero(cuda_dev, dt, D, T):
+def test_causal_from_zero(cuda_dev, kernel, dt, D, T):
     out, ref = _run(T, T, 8, 2, D, dt, cuda_dev, seed=T)
     assert max_abs_err(out, ref) < 2e-2
 
 
-@pytest.mark.parametrize("group", [1, 4, 8])
-def test_gqa_groups_with_prefix(cuda_dev, group):
+@pytest.mark.parametrize("group", [1, 2, 3, 4, 8])
+def test_gqa_groups_with_prefix(cuda_dev, kernel, group):
     # a 200-token chunk after a 333-token prefix: 533 keys, queries at 333..532
     out, ref = _run(200, 533, 2 * group, 2, 128, torch.bfloat16, cuda_dev, seed=group)
     assert max_abs_err(out, ref) < 2e-2
 
 
-def test_window_and_kv_start(cuda_dev):
+def test_window_and_kv_start(cuda_dev, kernel):
     out, ref = _run(150, 260, 8, 2, 64, torch.bfloat16, cuda_dev,
                     positions=np.arange(200, 350, dtype=np.int32), window=64, kv_start=100)
     assert max_abs_err(out, ref) < 2e-2
 
 
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16])
-def test_16bit_output(cuda_dev, out_dtype):
+def test_16bit_output(cuda_dev, kernel, out_dtype):
     out, ref = _run(256, 256, 4, 1, 128, torch.bfloat16, cuda_dev, out_dtype=out_dtype)
     assert max_abs_err(out, ref) < 2e-2
 
 
-def test_config2_shape(cuda_dev):
+def test_config2_shape(cuda_dev, kernel):
     """BASELINE config 2 geometry (S=2048, 32/8 heads, D=128, bf16, bf16 out)
     against the oracle on a subset of heads' rows (the oracle's fp32 einsum
     over all 32 heads x 2048^2 scores is too slow for a unit test)."""
@@ -85,7 +96,7 @@ def test_config2_shape(cuda_dev):
     assert max_abs_err(got, ref) < 2e-2
 
 
-def test_determinism(cuda_dev):
+def test_determinism(cuda_dev, kernel):
     from alpacca_open_sourced_by_jt_b200 import device
     q = torch.randn((384, 8, 128), device=cuda_dev, dtype=torch.bfloat16)
     k = torch.randn((384, 2, 128), device=cuda_dev, dtype=torch.bfloat16)
@@ -124,3 +135,27 @@ def test_qwen35_dropins(cuda_dev, golden):
     p = cases.qwen35_prefill()
     out = q35.qwen35_full_attention_prefill(p["q"], p["k"], p["v"], p["prefix"])
     assert max_abs_err(out, g["prefill_out"]) < 5e-3
+
+
+def test_long_prefix_multi_item_per_cta(cuda_dev):
+    """More work items than SMs (several items per persistent CTA), a long
+    prefix and a ragged last tile."""
+    out, ref = _run(1000, 3000, 32, 8, 128, torch.bfloat16, cuda_dev, seed=7)
+    assert max_abs_err(out, ref) < 2e-2
+
+
+def test_out_of_order_positions_are_reported(cuda_dev):
+    """The paired kernel takes a tile's key range from its first and last
+    query; positions that decrease inside a tile are outside that contract
+    and must be reported, not silently mis-masked."""
+    from alpacca_open_sourced_by_jt_b200 import _lib, device
+    _lib.device_error(clear=True)
+    T, H, KV, D = 128, 8, 2, 64
+    q = torch.randn((T, H, D), device=cuda_dev, dtype=torch.bfloat16)
+    k = torch.randn((400, KV, D), device=cuda_dev, dtype=torch.bfloat16)
+    v = torch.randn((400, KV, D), device=cuda_dev, dtype=torch.bfloat16)
+    pos = torch.arange(T, dtype=torch.int32, device=cuda_dev)
+    pos[5] = 399  # a row that sees keys past the tile's last position
+    device.prefill(q, k, v, pos)
+    code, aux = _lib.device_error(clear=True)
+    assert code == _lib.ERR_POSITION and aux == 5
