@@ -5,3 +5,4 @@
 #include "rope_append.cu"
 #include "prefill.cu"
 #include "prefill_pair.cu"
+#include "prefill_head.cu"

@@ -80,6 +80,17 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// A from TMEM (16-bit A: M rows on lanes, two K elements per 32-bit column,
+// K-major), B from shared memory.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void tc_ld32(uint32_t taddr, float* v) {
   uint32_t* r = reinterpret_cast<uint32_t*>(v);
   asm volatile(
@@ -102,6 +113,15 @@ __device__ __forceinline__ void tc_st32(uint32_t taddr, const float* v) {
       "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
       "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
       "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
       : "memory");
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -476,19 +496,35 @@ using b2a_host::fail;
 
 // Defined in prefill_pair.cu (same translation unit).
 template <typename T, typename TO, int D>
-int launch_prefill_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+int launch_prefill_pair(const void* q, const void* k, const void* v, const int* pos, void* out,
+                        int n_q, int t_kv, int H, int KV, float scale, int window, int kv_start,
+                        cudaStream_t st);
+
+template <typename T, typename TO, int D>
+int launch_prefill_head(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                         const int* pos, void* out, int n_q, int t_kv, int H, int KV, float scale,
                         int window, int kv_start, cudaStream_t st);
 
-// B2ATTN_PREFILL=single forces the one-tile kernel (for testing both paths).
-bool force_single_tile() {
+// Kernel choice.  Default: the paired-head persistent kernel
+// (prefill_pair.cu) for even GQA groups, the one-head persistent kernel
+// (prefill_head.cu) otherwise.  B2ATTN_PREFILL=head|pair|single forces one
+// (pair falls back to head for odd groups); the non-persistent one-tile
+// kernel below is kept as a tested reference schedule.
+enum class PrefillKernel { kHead, kPair, kSingle };
+PrefillKernel prefill_choice(int group) {
   const char* e = getenv("B2ATTN_PREFILL");
-  return e && strcmp(e, "single") == 0;
+  if (e && strcmp(e, "single") == 0) return PrefillKernel::kSingle;
+  if (e && strcmp(e, "head") == 0) return PrefillKernel::kHead;
+  return group % 2 == 0 ? PrefillKernel::kPair : PrefillKernel::kHead;
 }
 
 template <typename T, typename TO, int D>
 int launch_prefill(const void* q, const void* k, const void* v, const int* pos, void* out, int n_q,
                    int t_kv, int H, int KV, float scale, int window, int kv_start, cudaStream_t st) {
+  const PrefillKernel choice = prefill_choice(H / KV);
+  if (choice == PrefillKernel::kPair && (H / KV) % 2 == 0)
+    return launch_prefill_pair<T, TO, D>(q, k, v, pos, out, n_q, t_kv, H, KV, scale, window,
+                                         kv_start, st);
   const CUtensorMapDataType tdt = std::is_same<T, __nv_bfloat16>::value
                                       ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -504,8 +540,8 @@ int launch_prefill(const void* q, const void* k, const void* v, const int* pos, 
   if (rc) return rc;
   rc = b2a_host::make_tmap(&tv, tdt, 3, const_cast<void*>(v), kdims, kstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  if ((H / KV) % 2 == 0 && !force_single_tile())
-    return launch_prefill_pair<T, TO, D>(tq, tk, tv, pos, out, n_q, t_kv, H, KV, scale, window,
+  if (choice == PrefillKernel::kHead)
+    return launch_prefill_head<T, TO, D>(tq, tk, tv, pos, out, n_q, t_kv, H, KV, scale, window,
                                          kv_start, st);
   auto kern = prefill_kernel<T, TO, D>;
   // >= 116 KB keeps one CTA per SM, so the 512-column TMEM allocation never

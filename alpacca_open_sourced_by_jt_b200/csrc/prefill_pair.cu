@@ -1,7 +1,7 @@
 // Causal flash prefill, paired-head persistent kernel (tcgen05 + TMEM + TMA).
 //
 // Same math and masking as prefill.cu's prefill_kernel (the reference's
-// alpaccaroo/model.py:1254-1272 and :1567-1592); this kernel is the faster
+// alpaccaroo/model.py:1254-1272 and :1567-1592); this kernel is the fast
 // schedule for even GQA groups.
 //
 // Work item = (128-query tile, pair of query heads h0, h0+1 of one KV group).
@@ -13,22 +13,39 @@
 //   softmax B:            S1_j -> P1_j                      S1_{j+1} -> ...
 //
 // so each warpgroup's softmax runs while the tensor core works on the other
-// head's tile.  The grid is persistent (at most one CTA per SM); CTA c takes
-// items c, 2G-1-c, 2G+c, ... of the heaviest-first item list (snake order),
-// and the producer prefetches the next item's Q and K/V while the current
-// item drains.
+// head's tile.  P never touches shared memory: the softmax writes P_t(j) as
+// 16-bit pairs over the first 64 columns of S_t (after loading the whole
+// score row into registers) and PV reads it from TMEM (A operand in TMEM);
+// with both MMA operands and P in shared memory, its bandwidth, not the
+// tensor core, bounded the kernel.  Every tcgen05.mma is issued from
+// precomputed descriptors (one add per operand).
+//
+// The grid is persistent (at most one CTA per SM); CTA c takes items c,
+// 2G-1-c, 2G+c, ... of the heaviest-first item list (snake order), and the
+// producer prefetches the next item's Q and K/V while the current item drains.
 //
 // 384 threads:
-//   warp 0        TMA producer (Q pair, then K_j / V_j into a 3-slot ring)
+//   warp 0        TMA producer (Q pair, then K_j / V_j into a 5-slot ring)
 //   warp 1        TMEM owner, single-lane MMA issuer
 //   warps 2-3     idle
 //   warps 4-7     softmax warpgroup for head h0 (TMEM lanes = query rows)
 //   warps 8-11    softmax warpgroup for head h0+1
 // Registers: launched at 168 per thread (384 x 168 = 64512); the producer
-// warpgroup drops to 112 and the two softmax warpgroups rise to 184
-// (128 x 112 + 256 x 184 = 61440 <= 64512, the launch total).  The host
+// warpgroup drops to 120 and the two softmax warpgroups rise to 192
+// (128 x 120 + 256 x 192 = 64512, the launch total).  The host
 // refuses to launch if the compiled register count is not 168.
-// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [384,384+D).
+// TMEM (512 columns): S0/P0 [0,128) S1/P1 [128,256) O0 [256,256+D)
+// O1 [384,384+D).  SMEM (D=128): Q0, Q1 32 KB each, 5 K/V slots of 32 KB.
+//
+// Ordering facts the pipeline relies on (tcgen05.commit arrives only when
+// every MMA the issuing thread issued before it has completed):
+//   * QK_t(j+1) is issued after PV_t(j), so when S_t(j+1) is ready, PV_t(j)
+//     has read P_t(j) and its columns may be overwritten;
+//   * PV_t(j) is issued only after the softmax released P_t(j); a softmax
+//     that must rescale O_t (rare: its running max grew by more than 2^8)
+//     first waits for PV_t(j-1).  PV g of head t arrives on pv[t][g & 1],
+//     phase g >> 1, so skipped waits never make a parity wait ambiguous
+//     (PV g+2 needs P g+2, which the waiting softmax has not released).
 //
 // Positions must be non-decreasing within each 128-token tile (a prefill
 // chunk's positions always are): the key range of a tile is taken from its
@@ -51,15 +68,17 @@ using prefill::tc_fence_after;
 using prefill::tc_fence_before;
 using prefill::tc_ld32;
 using prefill::tc_mma;
+using prefill::tc_mma_ts;
+using prefill::tc_st16;
 using prefill::tc_st32;
 using prefill::tc_wait_ld;
 using prefill::tc_wait_st;
 
 constexpr int kThreads = 384;
-constexpr int kSlots = 3;
+constexpr int kSlots = 5;
 constexpr int kLaunchRegs = 168;
-constexpr int kProducerRegs = 112;
-constexpr int kSoftmaxRegs = 184;
+constexpr int kProducerRegs = 120;
+constexpr int kSoftmaxRegs = 192;
 // setmaxnreg.inc draws only on what the block was launched with
 static_assert(128 * kProducerRegs + 256 * kSoftmaxRegs <= kThreads * kLaunchRegs,
               "setmaxnreg split must fit in the launch allocation");
@@ -71,9 +90,7 @@ struct Layout {
   static constexpr int kQ0 = 0;
   static constexpr int kQ1 = kTile;
   static constexpr int kRing = 2 * kTile;
-  static constexpr int kP0 = kRing + kSlots * kTile;
-  static constexpr int kP1 = kP0 + (kBN / 64) * kBox;
-  static constexpr int kTotal = kP1 + (kBN / 64) * kBox;
+  static constexpr int kTotal = kRing + kSlots * kTile;
   static constexpr int kSmem = kTotal + 1024;
 };
 
@@ -120,7 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_qf, bar_qe;
   __shared__ __align__(8) uint64_t bar_full[kSlots], bar_empty[kSlots];
-  __shared__ __align__(8) uint64_t bar_sf[2], bar_pf[2], bar_pv[2], bar_oe[2];
+  __shared__ __align__(8) uint64_t bar_sf[2], bar_pf[2], bar_pv[2][2], bar_oe[2];
   __shared__ uint32_t s_tmem;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -138,7 +155,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bar_sf[t], 1);
       mbar_init(&bar_pf[t], 4);
-      mbar_init(&bar_pv[t], 1);
+      mbar_init(&bar_pv[t][0], 1);
+      mbar_init(&bar_pv[t][1], 1);
       mbar_init(&bar_oe[t], 4);
     }
     fence_mbar_init();
@@ -198,34 +216,35 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
       // ------------------------------ MMA issuer ---------------------------
       constexpr uint32_t idesc_qk = make_idesc<T>(kBM, kBN, false, false);
       constexpr uint32_t idesc_pv = make_idesc<T>(kBM, D, false, true);
-      const uint32_t sQ0 = smem_u32(smem + L::kQ0);
-      const uint32_t sQ1 = smem_u32(smem + L::kQ1);
-      const uint32_t sRing = smem_u32(smem + L::kRing);
-      const uint32_t sP0 = smem_u32(smem + L::kP0);
-      const uint32_t sP1 = smem_u32(smem + L::kP1);
+      // Descriptors precomputed once: the start address sits in the low 14
+      // bits (address >> 4), so a byte offset is an add of (off >> 4).
+      const uint64_t dQ[2] = {sw128_desc(smem_u32(smem + L::kQ0), 16, 1024),
+                              sw128_desc(smem_u32(smem + L::kQ1), 16, 1024)};
+      const uint64_t dK0 = sw128_desc(smem_u32(smem + L::kRing), 16, 1024);
+      const uint64_t dV0 = sw128_desc(smem_u32(smem + L::kRing), L::kBox, 1024);
+      constexpr uint64_t kSlotStep = L::kTile >> 4;
       uint32_t seq = 0, qcnt = 0, pcnt0 = 0, pcnt1 = 0;
+      uint32_t pvg[2] = {0, 0};  // PVs issued per head (running)
       bool ok = true;
       auto qk = [&](int t, uint32_t kslot) {
-        const uint32_t kb = sRing + kslot * L::kTile;
-        const uint32_t qb = t ? sQ1 : sQ0;
+        const uint64_t dk = dK0 + kslot * kSlotStep;
+        const uint64_t dq = dQ[t];
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * L::kBox + (kk & 3) * 32;
-          tc_mma(tmem + t * kBN, sw128_desc(qb + off, 16, 1024), sw128_desc(kb + off, 16, 1024),
-                 idesc_qk, kk > 0);
+          const uint64_t off = (((kk >> 2) * L::kBox) + (kk & 3) * 32) >> 4;
+          tc_mma(tmem + t * kBN, dq + off, dk + off, idesc_qk, kk > 0);
         }
         tc_commit(&bar_sf[t]);
       };
       auto pv = [&](int t, uint32_t vslot, bool acc) {
-        const uint32_t vb = sRing + vslot * L::kTile;
-        const uint32_t pb = t ? sP1 : sP0;
+        const uint64_t dv = dV0 + vslot * kSlotStep;
+        const uint32_t tp = tmem + t * kBN;  // P_t: 16 keys per 8 columns
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint32_t poff = (kk >> 2) * L::kBox + (kk & 3) * 32;
-          tc_mma(tmem + 2 * kBN + t * 128, sw128_desc(pb + poff, 16, 1024),
-                 sw128_desc(vb + kk * 16 * 128, L::kBox, 1024), idesc_pv, (acc || kk > 0));
-        }
-        tc_commit(&bar_pv[t]);
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          tc_mma_ts(tmem + 2 * kBN + t * 128, tp + kk * 8, dv + ((kk * 16 * 128) >> 4), idesc_pv,
+                    (acc || kk > 0));
+        tc_commit(&bar_pv[t][pvg[t] & 1]);
+        ++pvg[t];
       };
       for (int k = 0; ok; ++k) {
         const int idx = item_index(k, c, G);
@@ -283,8 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
     const int r = (warp & 3) * 32 + lane;         // query row within the tile == TMEM lane
     const uint32_t tl = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const uint32_t s_col = t * kBN, o_col = 2 * kBN + t * 128;
-    uint8_t* prow = smem + (t ? L::kP1 : L::kP0) + r * 128;
-    uint32_t scnt = 0, pvcnt = 0;
+    uint32_t scnt = 0, pvbase = 0;  // pvbase: this head's PVs before the item
     bool ok = true;
     for (int k = 0; ok; ++k) {
       const int idx = item_index(k, c, G);
@@ -357,32 +375,31 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
           m = mnew;
         }
         const float mref = (m == -INFINITY) ? 0.f : m;
-        // PV_t(j-1) was issued before QK_t(j), and tcgen05 MMAs complete in
-        // issue order, so this wait passes at once: P_t's buffer and O_t are
-        // free before any exponential is computed.
-        if (jj > 0) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&bar_pv[t], pvcnt & 1, 0x1A000 | jj));
-          if (!ok) break;
-          ++pvcnt;
-          tc_fence_after();
-        }
-        // exponentiate 8 scores at a time and store them straight into the
-        // swizzled P tile
+        // P_t(jj) as 16-bit pairs over the first 64 columns of S_t (the whole
+        // score row is in registers; PV_t(jj-1), the last reader of those
+        // columns, completed before QK_t(jj) did), 32 keys per store
         float suma = 0.f, sumb = 0.f;
 #pragma unroll
-        for (int ch = 0; ch < kBN / 8; ++ch) {
-          float p[8];
+        for (int qtr = 0; qtr < 4; ++qtr) {
+          uint32_t pk[16];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) p[e] = fast_exp2(fmaf(s[ch * 8 + e], sscale, -mref));
-          suma += (p[0] + p[1]) + (p[2] + p[3]);
-          sumb += (p[4] + p[5]) + (p[6] + p[7]);
-          *reinterpret_cast<uint4*>(prow + (ch >> 3) * L::kBox + (((ch & 7) ^ (r & 7)) << 4)) =
-              make_uint4(Pack2<T>::run(p[0], p[1]), Pack2<T>::run(p[2], p[3]),
-                         Pack2<T>::run(p[4], p[5]), Pack2<T>::run(p[6], p[7]));
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = fast_exp2(fmaf(s[qtr * 32 + 2 * e], sscale, -mref));
+            const float p1 = fast_exp2(fmaf(s[qtr * 32 + 2 * e + 1], sscale, -mref));
+            if (e & 1) sumb += p0 + p1; else suma += p0 + p1;
+            pk[e] = Pack2<T>::run(p0, p1);
+          }
+          tc_st16(tl + s_col + qtr * 16, pk);
         }
-        const float sum = suma + sumb;
-        l = l * alpha + sum;
+        tc_wait_st();
+        l = l * alpha + (suma + sumb);
+        // only an O rescale needs PV_t(jj-1) complete (PV_t(jj) is issued
+        // after this release, so it cannot race the rescale)
         if (warp_need && jj > 0) {
+          const uint32_t g = pvbase + jj - 1;
+          ok = __all_sync(0xffffffffu, mbar_wait(&bar_pv[t][g & 1], (g >> 1) & 1, 0x1A000 | jj));
+          if (!ok) break;
+          tc_fence_after();
 #pragma unroll
           for (int cc = 0; cc < D / 32; ++cc) {
             float o[32];
@@ -394,16 +411,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
           }
           tc_wait_st();
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar_pf[t]);
       }
       if (!ok) break;
-      // epilogue: wait for the last PV, O / l -> out, release O
-      ok = __all_sync(0xffffffffu, mbar_wait(&bar_pv[t], pvcnt & 1, 0x1B000));
+      // epilogue: wait for the last PV (every earlier one completed before
+      // it), O / l -> out, release O
+      {
+        const uint32_t g = pvbase + n - 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_pv[t][g & 1], (g >> 1) & 1, 0x1B000));
+      }
       if (!ok) break;
-      ++pvcnt;
+      pvbase += n;
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
@@ -437,9 +457,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
 namespace {
 
 template <typename T, typename TO, int D>
-int launch_prefill_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                        const int* pos, void* out, int n_q, int t_kv, int H, int KV, float scale,
-                        int window, int kv_start, cudaStream_t st) {
+int launch_prefill_pair(const void* q, const void* k, const void* v, const int* pos, void* out,
+                        int n_q, int t_kv, int H, int KV, float scale, int window, int kv_start,
+                        cudaStream_t st) {
   namespace P2 = b2a::prefill2;
   auto kern = P2::prefill_pair_kernel<T, TO, D>;
   cudaFuncAttributes fa;
@@ -450,7 +470,23 @@ int launch_prefill_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUte
                           "prefill_pair: compiled with %d registers/thread, the setmaxnreg split "
                           "needs exactly %d",
                           fa.numRegs, P2::kLaunchRegs);
-  const int smem = P2::Layout<D>::kSmem;
+  const CUtensorMapDataType tdt = std::is_same<T, __nv_bfloat16>::value
+                                      ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tq, tk, tv;
+  const uint64_t qdims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(H), static_cast<uint64_t>(n_q)};
+  const uint64_t qstr[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(H) * D * 2};
+  const uint64_t kdims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(KV), static_cast<uint64_t>(t_kv)};
+  const uint64_t kstr[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(KV) * D * 2};
+  const uint32_t box[3] = {64, 1, 128};
+  int rc = b2a_host::make_tmap(&tq, tdt, 3, const_cast<void*>(q), qdims, qstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = b2a_host::make_tmap(&tk, tdt, 3, const_cast<void*>(k), kdims, kstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = b2a_host::make_tmap(&tv, tdt, 3, const_cast<void*>(v), kdims, kstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  // >= 120 KB keeps one CTA per SM (a second one would wait for TMEM)
+  const int smem = P2::Layout<D>::kSmem > 120 * 1024 ? P2::Layout<D>::kSmem : 120 * 1024;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "cudaFuncSetAttribute(prefill_pair)");
   int dev = 0, sms = 148;
