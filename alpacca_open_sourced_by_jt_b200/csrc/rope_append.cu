@@ -1,8 +1,8 @@
 // Fused RoPE + KV-cache append.
 //
-// One CTA per token: bias add, rotation of the token's q heads (to q_out or
-// in place) and k heads, pass-through of the dims past n_rot, and the k/v
-// rows stored into the cache at the token's absolute position.  Positions
+// One CTA per (token, head slot): bias add, rotation of the token's q heads
+// (to q_out or in place) and k heads, pass-through of the dims past n_rot,
+// and the k/v rows stored into the cache at the token's absolute position.  Positions
 // are read from device memory, so the launch is identical from token to
 // token and can live inside a captured CUDA graph.
 //
@@ -26,9 +26,13 @@
 namespace b2a {
 namespace rope {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 128;
 constexpr int kMaxPairs = 128;  // head_dim <= 256
 
+// Grid (token, head slot): slots [0, H) are the token's q heads, [H, H+KV)
+// its k heads, [H+KV, H+2KV) its v heads.  Thread i of a q/k slot handles
+// rotation pair i (i < n_rot/2) or the two pass-through dims
+// n_rot + 2(i - n_rot/2), +1; thread i of a v slot copies dims 2i, 2i+1.
 template <typename TK, typename TQ>
 __global__ void __launch_bounds__(kThreads) rope_append_kernel(
     float* __restrict__ q, long long q_tok_stride, const float* __restrict__ k,
@@ -39,67 +43,60 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(
     TK* __restrict__ v_cache, long long seq_stride, int n_ctx, TQ* __restrict__ q_out,
     long long qo_tok_stride, int H, int KV, int D, int n_rot, int neox) {
   const int i = blockIdx.x;
+  const int slot = blockIdx.y;
   const int p = pos[i];
   if (p < 0 || p >= n_ctx || p >= tab_rows) {
-    if (threadIdx.x == 0) set_dev_error(B2A_ERR_POSITION, i);
+    if (threadIdx.x == 0 && slot == 0) set_dev_error(B2A_ERR_POSITION, i);
     return;
   }
   const int half = n_rot >> 1;
   const size_t seq = tok_seq_mode ? static_cast<size_t>(i) : 0;
-  const float* qi = q + i * q_tok_stride;
-  const float* ki = k + i * k_tok_stride;
-  const float* vi = v + i * v_tok_stride;
-  const float* cr = cos_tab + static_cast<size_t>(p) * half;
-  const float* sr = sin_tab + static_cast<size_t>(p) * half;
   TK* krow = k_cache + seq * seq_stride + static_cast<size_t>(p) * KV * D;
   TK* vrow = v_cache + seq * seq_stride + static_cast<size_t>(p) * KV * D;
-  TQ* qo = q_out + i * qo_tok_stride;  // the q row itself when rotating in place
-  const int nheads = H + KV;
-  const int npair = nheads * half;
-  const int tail = D - n_rot;
-  const int ntail = nheads * tail;
-  const int nv = KV * D;
-  for (int j = threadIdx.x; j < npair + ntail + nv; j += kThreads) {
-    if (j < npair) {
-      const int hh = j / half, jj = j - hh * half;
-      const int a = neox ? jj : 2 * jj;
-      const int b = neox ? jj + half : 2 * jj + 1;
-      const bool is_q = hh < H;
-      const int head = is_q ? hh : hh - H;
-      const float* src = is_q ? qi + head * D : ki + head * D;
-      const float* bias = is_q ? (bq ? bq + head * D : nullptr) : (bk ? bk + head * D : nullptr);
-      float x0 = src[a], x1 = src[b];
-      if (bias) {
-        x0 = __fadd_rn(x0, bias[a]);
-        x1 = __fadd_rn(x1, bias[b]);
+  for (int t = threadIdx.x; t < (D >> 1); t += blockDim.x) {
+    if (slot >= H + KV) {  // v row: plain copy (+ bias)
+      const int head = slot - H - KV;
+      const float* vi = v + i * v_tok_stride + head * D;
+      float x0 = vi[2 * t], x1 = vi[2 * t + 1];
+      if (bv) {
+        x0 = __fadd_rn(x0, bv[head * D + 2 * t]);
+        x1 = __fadd_rn(x1, bv[head * D + 2 * t + 1]);
       }
-      const float c = cr[jj], s = sr[jj];
-      const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-      const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-      if (is_q) {
-        st_elem(qo + head * D + a, y0);
-        st_elem(qo + head * D + b, y1);
-      } else {
-        st_elem(krow + head * D + a, y0);
-        st_elem(krow + head * D + b, y1);
-      }
-    } else if (j < npair + ntail) {
-      const int t = j - npair;
-      const int hh = t / tail, dd = n_rot + (t - hh * tail);
-      const bool is_q = hh < H;
-      const int head = is_q ? hh : hh - H;
-      float x = is_q ? qi[head * D + dd] : ki[head * D + dd];
-      const float* bias = is_q ? bq : bk;
-      if (bias) x = __fadd_rn(x, bias[head * D + dd]);
-      if (is_q)
-        st_elem(qo + head * D + dd, x);
-      else
-        st_elem(krow + head * D + dd, x);
+      st_elem(vrow + head * D + 2 * t, x0);
+      st_elem(vrow + head * D + 2 * t + 1, x1);
+      continue;
+    }
+    const bool is_q = slot < H;
+    const int head = is_q ? slot : slot - H;
+    const float* src = is_q ? q + i * q_tok_stride + head * D : k + i * k_tok_stride + head * D;
+    const float* bias = is_q ? (bq ? bq + head * D : nullptr) : (bk ? bk + head * D : nullptr);
+    int a, b;
+    if (t < half) {
+      a = neox ? t : 2 * t;
+      b = neox ? t + half : 2 * t + 1;
     } else {
-      const int t = j - npair - ntail;
-      float x = vi[t];
-      if (bv) x = __fadd_rn(x, bv[t]);
-      st_elem(vrow + t, x);
+      a = n_rot + 2 * (t - half);
+      b = a + 1;
+    }
+    float x0 = src[a], x1 = src[b];
+    if (bias) {
+      x0 = __fadd_rn(x0, bias[a]);
+      x1 = __fadd_rn(x1, bias[b]);
+    }
+    float y0 = x0, y1 = x1;
+    if (t < half) {
+      const float c = cos_tab[static_cast<size_t>(p) * half + t];
+      const float sn = sin_tab[static_cast<size_t>(p) * half + t];
+      y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+      y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    }
+    if (is_q) {
+      TQ* qo = q_out + i * qo_tok_stride + head * D;  // the q row itself when in place
+      st_elem(qo + a, y0);
+      st_elem(qo + b, y1);
+    } else {
+      st_elem(krow + head * D + a, y0);
+      st_elem(krow + head * D + b, y1);
     }
   }
 }
@@ -110,6 +107,8 @@ struct ImropeParams {
   int pairs;                         // P
 };
 
+// Same (token, head slot) grid; thread j of a q/k slot handles IMROPE pair
+// j < P (dims j, j + P) or, past P, the pass-through dims 2P + 2(j - P), +1.
 template <typename TK, typename TQ>
 __global__ void __launch_bounds__(kThreads) imrope_append_kernel(
     const float* __restrict__ q, long long q_tok_stride, const float* __restrict__ k,
@@ -119,59 +118,55 @@ __global__ void __launch_bounds__(kThreads) imrope_append_kernel(
     TK* __restrict__ v_cache, long long seq_stride, int n_ctx, TQ* __restrict__ q_out, int H,
     int KV, int D) {
   const int i = blockIdx.x;
+  const int slot = blockIdx.y;
   const int p = pos[i];
   if (p < 0 || p >= n_ctx) {
-    if (threadIdx.x == 0) set_dev_error(B2A_ERR_POSITION, i);
+    if (threadIdx.x == 0 && slot == 0) set_dev_error(B2A_ERR_POSITION, i);
     return;
   }
   const int P = prm.pairs;
   const size_t seq = tok_seq_mode ? static_cast<size_t>(i) : 0;
-  const float* qi = q + i * q_tok_stride;
-  const float* ki = k + i * k_tok_stride;
-  const float* vi = v + i * v_tok_stride;
   const int* ln = lanes + 4 * i;
   TK* krow = k_cache + seq * seq_stride + static_cast<size_t>(p) * KV * D;
   TK* vrow = v_cache + seq * seq_stride + static_cast<size_t>(p) * KV * D;
-  TQ* qo = q_out + static_cast<size_t>(i) * H * D;
-  const int nheads = H + KV;
-  const int npair = nheads * P;
-  const int tail = D - 2 * P;
-  const int ntail = nheads * tail;
-  const int nv = KV * D;
-  for (int j = threadIdx.x; j < npair + ntail + nv; j += kThreads) {
-    if (j < npair) {
-      const int hh = j / P, jj = j - hh * P;
-      const bool is_q = hh < H;
-      const int head = is_q ? hh : hh - H;
-      const float* src = is_q ? qi + head * D : ki + head * D;
+  for (int t = threadIdx.x; t < (D >> 1); t += blockDim.x) {
+    if (slot >= H + KV) {
+      const int head = slot - H - KV;
+      const float* vi = v + i * v_tok_stride + head * D;
+      st_elem(vrow + head * D + 2 * t, vi[2 * t]);
+      st_elem(vrow + head * D + 2 * t + 1, vi[2 * t + 1]);
+      continue;
+    }
+    const bool is_q = slot < H;
+    const int head = is_q ? slot : slot - H;
+    const float* src = is_q ? q + i * q_tok_stride + head * D : k + i * k_tok_stride + head * D;
+    TQ* qo = q_out + static_cast<size_t>(i) * H * D + head * D;
+    if (t < P) {
       const double theta =
-          __dmul_rn(__dmul_rn(static_cast<double>(ln[prm.lane[jj]]), freq_scale), prm.pw[jj]);
-      double s, c;
-      sincos(theta, &s, &c);
-      const double x0 = src[jj], x1 = src[jj + P];
+          __dmul_rn(__dmul_rn(static_cast<double>(ln[prm.lane[t]]), freq_scale), prm.pw[t]);
+      double sn, c;
+      sincos(theta, &sn, &c);
+      const double x0 = src[t], x1 = src[t + P];
       // separately rounded double products/sums, as Python floats do
-      const float y0 = static_cast<float>(__dsub_rn(__dmul_rn(x0, c), __dmul_rn(x1, s)));
-      const float y1 = static_cast<float>(__dadd_rn(__dmul_rn(x0, s), __dmul_rn(x1, c)));
+      const float y0 = static_cast<float>(__dsub_rn(__dmul_rn(x0, c), __dmul_rn(x1, sn)));
+      const float y1 = static_cast<float>(__dadd_rn(__dmul_rn(x0, sn), __dmul_rn(x1, c)));
       if (is_q) {
-        st_elem(qo + head * D + jj, y0);
-        st_elem(qo + head * D + jj + P, y1);
+        st_elem(qo + t, y0);
+        st_elem(qo + t + P, y1);
       } else {
-        st_elem(krow + head * D + jj, y0);
-        st_elem(krow + head * D + jj + P, y1);
+        st_elem(krow + head * D + t, y0);
+        st_elem(krow + head * D + t + P, y1);
       }
-    } else if (j < npair + ntail) {
-      const int t = j - npair;
-      const int hh = t / tail, dd = 2 * P + (t - hh * tail);
-      const bool is_q = hh < H;
-      const int head = is_q ? hh : hh - H;
-      const float x = is_q ? qi[head * D + dd] : ki[head * D + dd];
-      if (is_q)
-        st_elem(qo + head * D + dd, x);
-      else
-        st_elem(krow + head * D + dd, x);
     } else {
-      const int t = j - npair - ntail;
-      st_elem(vrow + t, vi[t]);
+      const int a = 2 * P + 2 * (t - P);
+      if (a >= D) continue;
+      if (is_q) {
+        st_elem(qo + a, src[a]);
+        st_elem(qo + a + 1, src[a + 1]);
+      } else {
+        st_elem(krow + head * D + a, src[a]);
+        st_elem(krow + head * D + a + 1, src[a + 1]);
+      }
     }
   }
 }
@@ -191,6 +186,13 @@ using R::rope_append_kernel;
 using R::imrope_append_kernel;
 using b2a_host::fail;
 
+// Threads per (token, head slot) CTA: one per element pair, in whole warps.
+int rope_block(int D) {
+  const int pairs = D / 2;
+  const int t = ((pairs + 31) / 32) * 32;
+  return t < R::kThreads ? t : R::kThreads;
+}
+
 // IMROPE lane schedule of one rotary pair (qwen35_ops.py:138-156).
 int imrope_lane(int pair, const int* sec) {
   const int total = sec[0] + sec[1] + sec[2] + sec[3];
@@ -207,7 +209,7 @@ void launch_rope(dim3 grid, cudaStream_t st, float* q, long long qs, const float
                  const float* ct, const float* stb, int tab_rows, const int* pos, int mode,
                  void* kc, void* vc, long long seq_stride, int n_ctx, void* q_out,
                  long long qos, int H, int KV, int D, int n_rot, int neox) {
-  rope_append_kernel<TK, TQ><<<grid, R::kThreads, 0, st>>>(
+  rope_append_kernel<TK, TQ><<<grid, rope_block(D), 0, st>>>(
       q, qs, k, ks, v, vs, bq, bk, bv, ct, stb, tab_rows, pos, mode, static_cast<TK*>(kc),
       static_cast<TK*>(vc), seq_stride, n_ctx, static_cast<TQ*>(q_out), qos, H, KV, D, n_rot,
       neox);
@@ -242,7 +244,7 @@ void launch_imrope(dim3 grid, cudaStream_t st, const float* q, long long qs, con
                    long long ks, const float* v, long long vs, const int* lanes,
                    const ImropeParams& prm, double fscale, const int* pos, int mode, void* kc,
                    void* vc, long long seq_stride, int n_ctx, void* q_out, int H, int KV, int D) {
-  imrope_append_kernel<TK, TQ><<<grid, R::kThreads, 0, st>>>(
+  imrope_append_kernel<TK, TQ><<<grid, rope_block(D), 0, st>>>(
       q, qs, k, ks, v, vs, lanes, prm, fscale, pos, mode, static_cast<TK*>(kc),
       static_cast<TK*>(vc), seq_stride, n_ctx, static_cast<TQ*>(q_out), H, KV, D);
 }
@@ -309,7 +311,8 @@ int b2a_rope_append(float* q, long long q_tok_stride, const float* k, long long 
     qos = q_tok_stride;
   }
   if (n_tok == 0) return B2A_OK;
-  dim3 grid(n_tok);
+  if (D & 1) return fail(B2A_ERR_SHAPE, "rope_append: head_dim %d must be even", D);
+  dim3 grid(n_tok, H + 2 * KV);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int neox = style == B2A_ROPE_NEOX;
   switch (kv_dtype) {
@@ -363,7 +366,8 @@ int b2a_imrope_append(const float* q, long long q_tok_stride, const float* k,
     prm.lane[j] = static_cast<signed char>(imrope_lane(j, sections));
   }
   if (n_tok == 0) return B2A_OK;
-  dim3 grid(n_tok);
+  if (D & 1) return fail(B2A_ERR_SHAPE, "imrope_append: head_dim %d must be even", D);
+  dim3 grid(n_tok, H + 2 * KV);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (kv_dtype) {
     case B2A_F32:

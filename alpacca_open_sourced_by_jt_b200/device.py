@@ -170,6 +170,26 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, positions: torch.
 _STYLE = {"norm": _lib.ROPE_NORM, "neox": _lib.ROPE_NEOX}
 
 
+def rope_tables(n_ctx: int, n_rot: int, rope_base: float, freq_scale: float = 1.0,
+                device=None):
+    """The cos/sin tables (n_ctx, n_rot/2) float32 that rope_append reads.
+
+    Built once per model on the host, in float32 as the reference's model
+    set-up builds them (alpaccaroo/model.py:318-323 for inv_freq =
+    freq_scale * base^(-2i/n_rot) over a float32 index, :871-875 for
+    theta = position * inv_freq and its cos/sin), so the rotations agree
+    with the reference bit for bit; then copied to `device` (default: the
+    current CUDA device).  Set-up only, not part of the per-token path."""
+    import numpy as np
+    _need(n_rot > 0 and n_rot % 2 == 0, "n_rot must be even and positive")
+    f32 = np.float32
+    idx = np.arange(n_rot // 2, dtype=f32)
+    inv = f32(freq_scale) * np.power(f32(rope_base), idx * f32(-2.0) / f32(n_rot))
+    theta = np.arange(n_ctx, dtype=f32)[:, None] * inv[None, :]
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    return (torch.from_numpy(np.cos(theta)).to(dev), torch.from_numpy(np.sin(theta)).to(dev))
+
+
 def rope_append(q: torch.Tensor, k: torch.Tensor | None, v: torch.Tensor | None,
                 positions: torch.Tensor, cos_tab: torch.Tensor, sin_tab: torch.Tensor, *,
                 k_cache=None, v_cache=None, n_rot: int | None = None, style: str = "norm",

@@ -13,6 +13,10 @@ Also reported on the same line:
   prefill   BASELINE config 2 causal prefill (S=2048, 32/8 heads, D=128,
             bf16 in/out) in TFLOP/s, flops = 4*H*D*S(S+1)/2, L2 flushed
             between launches (inputs are 24 MB)
+  varlen    BASELINE config 3: 64 sequences of ragged length (1K-8K), fp16
+            KV, fused RoPE+append then decode, GB/s
+  longctx   BASELINE config 4: 4 x 131072 rows split over the GPUs, NCCL
+            all-gather of (o, lse) parts + LSE combine, GB/s
   e2e       the decode step through the public API with host buffers: per
             step the pinned host q/k/v rows of the new token go H2D, the
             fused RoPE+append writes them into the resident cache, decode
@@ -46,6 +50,7 @@ METRIC = "decode-attn KV GB/s (% HBM peak) @32K ctx; prefill-attn TFLOPS; at 1/2
 WL = dict(B=16, L=32768, H=32, KV=8, D=128)            # decode workload (per rank)
 PF = dict(S=2048, H=32, KV=8, D=128)                   # prefill workload (config 2)
 LC = dict(B=4, L=131072, H=64, KV=8, D=128)            # long-context split (config 4)
+VL = dict(B=64, Lmin=1024, Lmax=8192, H=32, KV=8, D=128)  # varlen batched decode (config 3)
 FALLBACK_HBM = 6650.0
 FALLBACK_BF16 = 1590.0
 SPEC_HBM = 8000.0
@@ -239,15 +244,79 @@ def bench_longctx(dev, rank, world, steps, warmup, dist):
                       "B*H*(D+1) f32 per rank, LSE-combine kernel"}
 
 
+def bench_varlen(dev, rank, world, steps, warmup, dist):
+    """64 sequences per GPU with cached lengths
+    L_b ~ U[1024, 8192] (seed 2), 32 q / 8 KV heads, D=128, fp16 KV ~ N(0,1)
+    (seed 2 + rank).  One step is the device half of a batched decode token:
+    the fused RoPE + append kernel rotates every sequence's new q/k row at
+    position L_b and stores k/v there, then the split-KV decode (split +
+    combine kernels) attends over L_b + 1 rows.  Bytes per step: the KV rows
+    read, sum_b 2*(L_b+1)*KV*D*2, plus the new rows and q/out traffic."""
+    import numpy as np
+    import torch
+    from alpacca_open_sourced_by_jt_b200 import device
+    B, H, KV, D = VL["B"], VL["H"], VL["KV"], VL["D"]
+    Ls = np.random.default_rng(2).integers(VL["Lmin"], VL["Lmax"] + 1, size=B)
+    n_ctx = VL["Lmax"] + 1
+    g = torch.Generator(device=dev).manual_seed(2 + rank)
+    kc = torch.randn((B, n_ctx, KV, D), device=dev, dtype=torch.float16, generator=g)
+    vc = torch.randn((B, n_ctx, KV, D), device=dev, dtype=torch.float16, generator=g)
+    q = torch.randn((B, H, D), device=dev, dtype=torch.float32, generator=g)
+    kn = torch.randn((B, KV, D), device=dev, dtype=torch.float32, generator=g)
+    vn = torch.randn((B, KV, D), device=dev, dtype=torch.float32, generator=g)
+    qr = torch.empty_like(q)
+    out = torch.empty_like(q)
+    pos = torch.from_numpy(Ls.astype(np.int32)).to(dev)
+    lens = pos + 1
+    ct, stt = device.rope_tables(n_ctx, D, 500000.0, device=dev)
+    split = device.decode_split_rows(B, KV, n_ctx, torch.float16)
+    ws = device.decode_workspace(B, H, D, n_ctx, split, dev)
+
+    def step():
+        device.rope_append(q, kn, vn, pos, ct, stt, k_cache=kc, v_cache=vc, per_sequence=True,
+                           q_out=qr)
+        device.decode(qr, kc, vc, lens, out=out, workspace=ws, split_rows=split, max_len=n_ctx)
+
+    for _ in range(max(warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    nsteps = max(10, min(steps, 1000))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(nsteps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    kv_bytes = int(sum(2 * (int(L) + 1) * KV * D * 2 for L in Ls))
+    extra = B * 2 * KV * D * (4 + 2) + B * H * D * 4 * 4   # new rows in/out; q, q_rot x2, out
+    per_step = kv_bytes + extra
+    del kc, vc
+    return {"metric": "varlen batched decode GB/s (config 3)",
+            "value": round(world * per_step / (ms / nsteps * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "ms_per_step": round(ms / nsteps, 4), "steps": nsteps, "n_gpus": world,
+            "scaling": "weak", "bytes_per_step_per_gpu": per_step, "split_rows": split,
+            "gpu_launches_per_step": 3,
+            "config": "64 seqs per GPU, L_b ~ U[1024,8192] (seed 2; mean "
+                      f"{float(Ls.mean()):.0f}), 32 q / 8 KV heads, D=128, fp16 KV; per step: "
+                      "fused RoPE+append of each new token at L_b, split-KV decode over "
+                      "L_b+1 rows; KV bytes > L2, no flush"}
+
+
 def bench_e2e(dev, st, steps, warmup):
     """Decode step through the public API with host buffers (see module doc)."""
     import numpy as np
     import torch
-    import oracle
     from alpacca_open_sourced_by_jt_b200 import device
     B, L, H, KV, D = WL["B"], WL["L"], WL["H"], WL["KV"], WL["D"]
-    cos, sin = oracle.rope_tables(L, D, 500000.0)
-    ct, stt = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+    ct, stt = device.rope_tables(L, D, 500000.0, device=dev)
     rng = np.random.default_rng(7)
     h_q = torch.from_numpy(rng.standard_normal((B, H, D), dtype=np.float32)).pin_memory()
     h_k = torch.from_numpy(rng.standard_normal((B, KV, D), dtype=np.float32)).pin_memory()
@@ -385,6 +454,9 @@ def run_ours(args):
     lc = None
     if args.only in (None, "longctx"):
         lc = bench_longctx(dev, rank, world, args.steps, args.warmup, dist)
+    vl = None
+    if args.only in (None, "varlen"):
+        vl = bench_varlen(dev, rank, world, args.steps, args.warmup, dist)
     ms = st["ms"]
     if dist is not None:
         t = torch.tensor([ms], device=dev)
@@ -430,6 +502,11 @@ def run_ours(args):
             result["e2e"] = e2e
         if lc:
             result["longctx"] = lc
+        if vl:
+            vl["roofline"] = {"bound": "hbm", "achieved": round(vl["value"] / world, 1),
+                              "peak": hbm, "unit": "GB/s",
+                              "frac": round(vl["value"] / world / hbm, 4)}
+            result["varlen"] = vl
         if cpu:
             result["cpu_baseline"] = cpu
         if clk:
@@ -510,7 +587,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
-    ap.add_argument("--only", choices=["decode", "e2e", "prefill", "longctx"], default=None,
+    ap.add_argument("--only", choices=["decode", "e2e", "prefill", "longctx", "varlen"],
+                    default=None,
                     help="profiling aid: run the decode timing plus only this extra part")
     ap.add_argument("--batch", type=int, default=WL["B"],
                     help="profiling aid: sequences per GPU (default 16)")
