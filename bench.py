@@ -521,7 +521,9 @@ def run_ours(args):
                 "roofline": {"bound": "tensor", "achieved": round(pf["tflops"], 1),
                              "peak": bf16, "unit": "TFLOP/s",
                              "frac": round(pf["tflops"] / bf16, 4),
-                             "traffic": profiled_traffic("prefill_kernel bf16 D128"),
+                             "traffic": profiled_traffic("prefill_pair_kernel bf16 D128"),
+                             "kernel": "prefill_pair_kernel<bf16,bf16,128> (default for even "
+                                       "GQA groups)",
                              "peak_source": f"{src} (MEASURED_PEAKS.json bf16_tflops, burst)"},
                 "launches": pf["launches"]}
             if pcpu:
