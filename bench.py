@@ -17,10 +17,11 @@ Also reported on the same line:
             KV, fused RoPE+append then decode, GB/s
   longctx   BASELINE config 4: 4 x 131072 rows split over the GPUs, NCCL
             all-gather of (o, lse) parts + LSE combine, GB/s
-  e2e       the decode step through the public API with host buffers: per
-            step the pinned host q/k/v rows of the new token go H2D, the
-            fused RoPE+append writes them into the resident cache, decode
-            runs, the output comes back D2H and the host waits for it
+  e2e       the decode step through the public API with host buffers
+            (DecodeStep, one CUDA graph per token): per step the pinned host
+            q/k/v rows and positions go H2D, the fused RoPE+append writes
+            them into the resident cache, decode runs, the output comes back
+            D2H and the host waits for it
   roofline  decode against MEASURED_PEAKS.json's copy bandwidth
   cpu_baseline  the reference's NumPy decode (oracle port) on host cores
 
@@ -311,46 +312,37 @@ def bench_varlen(dev, rank, world, steps, warmup, dist):
 
 
 def bench_e2e(dev, st, steps, warmup):
-    """Decode step through the public API with host buffers (see module doc)."""
+    """Decode step through the public API with host buffers (see module doc):
+    DecodeStep replays the whole step (H2D of the pinned rows, fused
+    RoPE+append, decode, D2H of the output) as one CUDA graph per token."""
     import numpy as np
     import torch
     from alpacca_open_sourced_by_jt_b200 import device
+    from alpacca_open_sourced_by_jt_b200.decode_step import DecodeStep
     B, L, H, KV, D = WL["B"], WL["L"], WL["H"], WL["KV"], WL["D"]
     ct, stt = device.rope_tables(L, D, 500000.0, device=dev)
     rng = np.random.default_rng(7)
-    h_q = torch.from_numpy(rng.standard_normal((B, H, D), dtype=np.float32)).pin_memory()
-    h_k = torch.from_numpy(rng.standard_normal((B, KV, D), dtype=np.float32)).pin_memory()
-    h_v = torch.from_numpy(rng.standard_normal((B, KV, D), dtype=np.float32)).pin_memory()
-    h_out = torch.empty((B, H, D), dtype=torch.float32).pin_memory()
-    d_q = torch.empty_like(h_q, device=dev)
-    d_k = torch.empty_like(h_k, device=dev)
-    d_v = torch.empty_like(h_v, device=dev)
-    pos = torch.full((B,), L - 1, dtype=torch.int32, device=dev)
-    kc, vc, lens, ws, out, split = st["kc"], st["vc"], st["lens"], st["ws"], st["out"], st["split"]
-
-    def step():
-        d_q.copy_(h_q, non_blocking=True)
-        d_k.copy_(h_k, non_blocking=True)
-        d_v.copy_(h_v, non_blocking=True)
-        device.rope_append(d_q, d_k, d_v, pos, ct, stt, k_cache=kc, v_cache=vc,
-                           per_sequence=True)
-        device.decode(d_q, kc, vc, lens, out=out, workspace=ws, split_rows=split, max_len=L)
-        h_out.copy_(out, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+    step = DecodeStep(st["kc"], st["vc"], ct, stt, H)
+    step.q.copy_(torch.from_numpy(rng.standard_normal((B, H, D), dtype=np.float32)))
+    step.k.copy_(torch.from_numpy(rng.standard_normal((B, KV, D), dtype=np.float32)))
+    step.v.copy_(torch.from_numpy(rng.standard_normal((B, KV, D), dtype=np.float32)))
+    step.positions.fill_(L - 1)
 
     for _ in range(max(warmup, 3)):
         step()
     n = max(3, min(steps, 500))
     t0 = time.perf_counter()
     for _ in range(n):
-        step()
+        out = step()
     dt = time.perf_counter() - t0
     bytes_step = decode_bytes(B, L, KV, D)
     return dict(value=bytes_step / (dt / n) / 1e9, unit="GB/s",
-                h2d_bytes_per_step=int(h_q.numel() * 4 + h_k.numel() * 4 + h_v.numel() * 4),
-                d2h_bytes_per_step=int(h_out.numel() * 4), steps=n,
+                h2d_bytes_per_step=int((B * H * D + 2 * B * KV * D) * 4 + 2 * B * 4),
+                d2h_bytes_per_step=int(out.numel() * 4), steps=n,
                 ms_per_step=dt / n * 1e3,
-                path="rope_append + decode with resident cache, pinned host q/k/v in, out back")
+                path="DecodeStep: one CUDA graph per token (pinned q/k/v/positions H2D, "
+                     "fused RoPE+append into the resident cache, split-KV decode, output "
+                     "D2H), host waits for each step")
 
 
 def bench_prefill(dev, steps, warmup):
