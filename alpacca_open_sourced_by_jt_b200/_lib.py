@@ -69,6 +69,7 @@ SIGNATURES = [
                                   c_longlong, c_void_p, POINTER(c_int), c_double, c_double,
                                   c_void_p, c_int, c_void_p, c_void_p, c_longlong, c_int, c_int,
                                   c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p]),
+    ("b2a_kv_convert", c_int, [c_void_p, c_int, c_void_p, c_int, c_longlong, c_void_p]),
 ]
 
 _lib = None

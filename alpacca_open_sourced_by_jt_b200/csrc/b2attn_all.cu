@@ -6,3 +6,4 @@
 #include "prefill.cu"
 #include "prefill_pair.cu"
 #include "prefill_head.cu"
+#include "kvconvert.cu"

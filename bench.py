@@ -17,6 +17,8 @@ Also reported on the same line:
             KV, fused RoPE+append then decode, GB/s
   longctx   BASELINE config 4: 4 x 131072 rows split over the GPUs, NCCL
             all-gather of (o, lse) parts + LSE combine, GB/s
+  kvstate   KV state boundary: device widening/narrowing of one 32K-row bf16
+            layer (HBM GB/s) and a whole-layer f32 snapshot
   e2e       the decode step through the public API with host buffers
             (DecodeStep, one CUDA graph per token): per step the pinned host
             q/k/v rows and positions go H2D, the fused RoPE+append writes
@@ -311,6 +313,64 @@ def bench_varlen(dev, rank, world, steps, warmup, dist):
                       "L_b+1 rows; KV bytes > L2, no flush"}
 
 
+def bench_kvstate(dev, steps, warmup):
+    """KV state boundary (kvstate.py): one layer of one headline sequence's
+    cache, 32768 rows x 8 KV heads x 128, bf16.  Times b2a_kv_convert's
+    widening bf16 -> f32 (what a snapshot runs on the device) and the
+    narrowing f32 -> bf16 of a restore, each HBM-bound at 6 bytes per
+    element (2 read + 4 written or 4 read + 2 written, 201 MB per launch,
+    above L2); and a whole-layer snapshot (widen K and V, D2H, host bytes)."""
+    import torch
+    from alpacca_open_sourced_by_jt_b200.kvstate import DeviceAttentionState, convert
+    L, KV, D = 32768, 8, 128
+    st = DeviceAttentionState(0, KV, D, D, L, torch.bfloat16, dev)
+    g = torch.Generator(device=dev).manual_seed(11)
+    st.key.copy_(torch.randn(st.key.shape, generator=g, device=dev))
+    st.value.copy_(torch.randn(st.value.shape, generator=g, device=dev))
+    st.advance(L)
+    n = L * KV * D
+    k16 = st.key.reshape(-1)
+    f32 = torch.empty(n, dtype=torch.float32, device=dev)
+    k16b = torch.empty_like(k16)
+
+    def timed(fn, reps):
+        for _ in range(max(warmup, 3)):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    reps = max(10, min(steps, 200))
+    ms_w = timed(lambda: convert(k16, f32), reps)
+    ms_n = timed(lambda: convert(f32, k16b), reps)
+    assert torch.equal(k16b, k16)  # narrow(widen(x)) == x for 16-bit x
+    st.snapshot()
+    t0 = time.perf_counter()
+    for _ in range(3):
+        snap = st.snapshot()
+    ms_s = (time.perf_counter() - t0) / 3 * 1e3
+    hbm, _, _, src = peaks()
+    bytes_conv = n * 6
+    gbs_w = bytes_conv / (ms_w * 1e-3) / 1e9
+    return {"metric": "KV snapshot widening GB/s (b2a_kv_convert bf16 -> f32, HBM)",
+            "value": round(gbs_w, 1), "unit": "GB/s", "ms_per_launch": round(ms_w, 4),
+            "narrow_gbs": round(bytes_conv / (ms_n * 1e-3) / 1e9, 1),
+            "narrow_ms_per_launch": round(ms_n, 4),
+            "snapshot_layer_ms": round(ms_s, 2),
+            "snapshot_layer_gbs": round(snap.memory_bytes() / (ms_s * 1e-3) / 1e9, 2),
+            "roofline": {"bound": "hbm", "achieved": round(gbs_w, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(gbs_w / hbm, 4),
+                         "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)"},
+            "config": "one layer, 32768 rows x 8 KV heads x 128, bf16 cache; widening and "
+                      "narrowing timed back to back (201 MB per launch); snapshot = K and V "
+                      "widened on the device, copied to host f32-le bytes"}
+
+
 def bench_e2e(dev, st, steps, warmup):
     """Decode step through the public API with host buffers (see module doc):
     DecodeStep replays the whole step (H2D of the pinned rows, fused
@@ -449,6 +509,9 @@ def run_ours(args):
     vl = None
     if args.only in (None, "varlen"):
         vl = bench_varlen(dev, rank, world, args.steps, args.warmup, dist)
+    kvs = None
+    if rank == 0 and args.only in (None, "kvstate"):
+        kvs = bench_kvstate(dev, args.steps, args.warmup)
     ms = st["ms"]
     if dist is not None:
         t = torch.tensor([ms], device=dev)
@@ -494,6 +557,8 @@ def run_ours(args):
             result["e2e"] = e2e
         if lc:
             result["longctx"] = lc
+        if kvs:
+            result["kvstate"] = kvs
         if vl:
             vl["roofline"] = {"bound": "hbm", "achieved": round(vl["value"] / world, 1),
                               "peak": hbm, "unit": "GB/s",
@@ -581,7 +646,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
-    ap.add_argument("--only", choices=["decode", "e2e", "prefill", "longctx", "varlen"],
+    ap.add_argument("--only", choices=["decode", "e2e", "prefill", "longctx", "varlen",
+                                       "kvstate"],
                     default=None,
                     help="profiling aid: run the decode timing plus only this extra part")
     ap.add_argument("--batch", type=int, default=WL["B"],

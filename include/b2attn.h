@@ -194,6 +194,21 @@ int b2a_imrope_append(const float* q, long long q_tok_stride, const float* k,
                       void* v_cache, long long seq_stride, int n_ctx, int kv_dtype, void* q_out,
                       int q_out_dtype, int n_tok, int H, int KV, int D, void* stream);
 
+/* Convert n cache elements between storage types, on the device: widening
+ * a 16-bit cache to f32 (exact) for a snapshot or a host f32 mirror, and
+ * narrowing f32 rows to 16 bits (round to nearest even) for a restore or a
+ * mirror upload.  Replaces the host-side conversions around the reference's
+ * device KV mirror: the f32 -> f16 staging of _sync_mirror
+ * (alpaccaroo/cuda.py:1881-1900) and the f16 -> f32 widening of rows coming
+ * home after a device prefill chunk (cuda.py:2046-2061).  Snapshots keep
+ * the reference's f32-le row format (alpaccaroo/memory.py:224-241).
+ *
+ *   src, dst  device buffers of n elements (any of F32/F16/BF16 each; same
+ *             type is a copy); they must not overlap
+ * Returns B2A_OK or B2A_ERR_ARG / B2A_ERR_DTYPE / B2A_ERR_CUDA. */
+int b2a_kv_convert(const void* src, int src_dtype, void* dst, int dst_dtype, long long n,
+                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

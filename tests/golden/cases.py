@@ -110,3 +110,14 @@ def gqa_step_case():
     k = rng.standard_normal((7, 2, 16))
     v = rng.standard_normal((7, 2, 16))
     return dict(q=q, k=k, v=v, sha256=_digest(q, k, v))
+
+
+def kv_state_case():
+    """One attention layer's state: 37 appended K/V rows, 2 KV heads, key
+    and value dim 16, f32 N(0,1); truncated to 20 rows afterwards."""
+    rng = np.random.default_rng(21)
+    L, KV, D = 37, 2, 16
+    k = rng.standard_normal((L, KV, D), dtype=np.float32)
+    v = rng.standard_normal((L, KV, D), dtype=np.float32)
+    return dict(layer_index=3, L=L, KV=KV, D=D, truncate=20, k=k, v=v, sha256=_digest(k, v))
+

@@ -103,8 +103,31 @@ def make_qwen35(qk_mod, ops_mod):
                         gqa_sha256=g["sha256"], gqa_out=gqa)
 
 
+def make_kv_state():
+    """The reference's own attention-layer state (alpaccaroo/memory.py:385-475):
+    rows appended one at a time, snapshot, truncate, snapshot again."""
+    from alpaccaroo import memory  # noqa: WPS433
+    c = cases.kv_state_case()
+    spec = memory.LayerMemorySpec(layer_index=c["layer_index"], kind="attention",
+                                  kv_heads=c["KV"], key_dim=c["D"], value_dim=c["D"])
+    st = memory.FullAttentionState(spec)
+    for p in range(c["L"]):
+        st.append(c["k"][p].ravel().tolist(), c["v"][p].ravel().tolist())
+    full = st.snapshot()
+    st.truncate(c["truncate"])
+    cut = st.snapshot()
+    np.savez_compressed(
+        os.path.join(HERE, "kv_state.npz"), input_sha256=c["sha256"],
+        key=np.frombuffer(full.key, np.uint8), value=np.frombuffer(full.value, np.uint8),
+        length=full.logical_length, dtype=full.dtype, kind=full.kind,
+        memory_bytes=full.memory_bytes(),
+        key_cut=np.frombuffer(cut.key, np.uint8), value_cut=np.frombuffer(cut.value, np.uint8),
+        length_cut=cut.logical_length, memory_bytes_cut=cut.memory_bytes())
+
+
 def main():
     model_mod, qk_mod, ops_mod = _import_reference()
+    make_kv_state()
     make_decode_config1(model_mod)
     make_rope_neox(model_mod)
     make_prefill(model_mod)

@@ -118,3 +118,14 @@ def test_lse_combine_rejects_bad_arguments(lib):
     assert lib.b2a_lse_combine(None, 0, 16, 0, 2, 3, 4, 16, None, None) == _lib.ERR_ARG
     assert lib.b2a_lse_combine(16, 0, 16, 0, 0, 3, 4, 16, None, None) == _lib.ERR_ARG
     assert lib.b2a_lse_combine(16, 5, 16, 0, 2, 3, 4, 16, None, None) == _lib.ERR_SHAPE
+
+
+def test_kv_convert_rejects_bad_arguments(lib):
+    p, q = 1 << 20, 1 << 21  # never dereferenced: every case returns before a launch
+    assert lib.b2a_kv_convert(p, _lib.BF16, q, _lib.F32, 0, None) == _lib.OK
+    assert lib.b2a_kv_convert(None, _lib.BF16, q, _lib.F32, 8, None) == _lib.ERR_ARG
+    assert lib.b2a_kv_convert(p, _lib.BF16, None, _lib.F32, 8, None) == _lib.ERR_ARG
+    assert lib.b2a_kv_convert(p, _lib.BF16, q, _lib.F32, -1, None) == _lib.ERR_ARG
+    assert lib.b2a_kv_convert(p, 7, q, _lib.F32, 8, None) == _lib.ERR_DTYPE
+    assert lib.b2a_kv_convert(p, _lib.F16, q, 7, 8, None) == _lib.ERR_DTYPE
+    assert lib.b2a_kv_convert(p, _lib.F32, p + 16, _lib.F16, 8, None) == _lib.ERR_ARG  # overlap
