@@ -70,6 +70,13 @@ SIGNATURES = [
                                   c_void_p, c_int, c_void_p, c_void_p, c_longlong, c_int, c_int,
                                   c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p]),
     ("b2a_kv_convert", c_int, [c_void_p, c_int, c_void_p, c_int, c_longlong, c_void_p]),
+    ("b2a_qwen35_attn_prep", c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_void_p,
+                                     c_longlong, c_void_p, c_void_p, c_double, c_void_p,
+                                     POINTER(c_int), c_double, c_double, c_void_p, c_int,
+                                     c_void_p, c_void_p, c_longlong, c_int, c_int, c_void_p,
+                                     c_int, c_int, c_int, c_int, c_int, c_void_p]),
+    ("b2a_sigmoid_gate", c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_void_p,
+                                 c_longlong, c_int, c_int, c_void_p]),
 ]
 
 _lib = None

@@ -7,3 +7,4 @@
 #include "prefill_pair.cu"
 #include "prefill_head.cu"
 #include "kvconvert.cu"
+#include "qwen35_layer.cu"

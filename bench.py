@@ -19,6 +19,8 @@ Also reported on the same line:
             all-gather of (o, lse) parts + LSE combine, GB/s
   kvstate   KV state boundary: device widening/narrowing of one 32K-row bf16
             layer (HBM GB/s) and a whole-layer f32 snapshot
+  qwen35_layer  Qwen35 full-attention layer step (prologue, decode, gate) at
+            16 x 32K rows, 16/2 heads, head_dim 256, bf16, GB/s
   e2e       the decode step through the public API with host buffers
             (DecodeStep, one CUDA graph per token): per step the pinned host
             q/k/v rows and positions go H2D, the fused RoPE+append writes
@@ -371,6 +373,60 @@ def bench_kvstate(dev, steps, warmup):
                       "widened on the device, copied to host f32-le bytes"}
 
 
+def bench_qwen35(dev, steps, warmup):
+    """Qwen35 full-attention layer step (qwen35_layer.py) at a Qwen3.5-style
+    shape: 16 sequences x 32768 cached rows, 16 q / 2 KV heads, head_dim 256,
+    IMROPE sections (11, 11, 10, 0), bf16 cache.  One step = prologue (split,
+    RMSNorm, IMROPE, append), split-KV decode, sigmoid gate; bytes = the KV
+    rows read plus the rows and activations moved (HBM-bound)."""
+    import numpy as np
+    import torch
+    from alpacca_open_sourced_by_jt_b200.qwen35_layer import Qwen35AttentionLayer
+    B, L, H, KV, D = 16, 32768, 16, 2, 256
+    rng = np.random.default_rng(9)
+    lay = Qwen35AttentionLayer(query_heads=H, kv_heads=KV, head_dim=D, rms_epsilon=1e-6,
+                               rope_freq_base=1e7, sections=(11, 11, 10, 0),
+                               query_norm=np.ones(D, np.float32),
+                               key_norm=np.ones(D, np.float32), n_ctx=L + 1, batch=B,
+                               kv_dtype=torch.bfloat16, device_=dev)
+    g = torch.Generator(device=dev).manual_seed(9)
+    lay.k_cache.copy_(torch.randn(lay.k_cache.shape, generator=g, device=dev))
+    lay.v_cache.copy_(torch.randn(lay.v_cache.shape, generator=g, device=dev))
+    qg = torch.from_numpy(rng.standard_normal((B, H * 2 * D), dtype=np.float32)).to(dev)
+    k = torch.from_numpy(rng.standard_normal((B, KV * D), dtype=np.float32)).to(dev)
+    v = torch.from_numpy(rng.standard_normal((B, KV * D), dtype=np.float32)).to(dev)
+    pos = torch.full((B,), L, dtype=torch.int32, device=dev)
+
+    def step():
+        lay.step(qg, k, v, pos)
+
+    for _ in range(max(warmup, 3)):
+        step()
+    n = max(10, min(steps, 500))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(n):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    kv_bytes = B * 2 * (L + 1) * KV * D * 2
+    extra = B * (H * 2 * D + 2 * KV * D) * 4 + B * H * D * 4 * 4
+    gbs = (kv_bytes + extra) / (ms * 1e-3) / 1e9
+    hbm, _, _, src = peaks()
+    del lay
+    return {"metric": "Qwen35 attention layer step GB/s", "value": round(gbs, 1), "unit": "GB/s",
+            "ms_per_step": round(ms, 4), "steps": n,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gbs / hbm, 4),
+                         "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)"},
+            "config": "16 seqs x 32768 cached rows, 16 q / 2 KV heads, head_dim 256, IMROPE "
+                      "(11,11,10,0), bf16 cache; per step: b2a_qwen35_attn_prep, b2a_decode "
+                      "(split + combine), b2a_sigmoid_gate (4 launches plus 2 small torch ops "
+                      "for lanes and lengths)"}
+
+
 def bench_e2e(dev, st, steps, warmup):
     """Decode step through the public API with host buffers (see module doc):
     DecodeStep replays the whole step (H2D of the pinned rows, fused
@@ -512,6 +568,9 @@ def run_ours(args):
     kvs = None
     if rank == 0 and args.only in (None, "kvstate"):
         kvs = bench_kvstate(dev, args.steps, args.warmup)
+    q35 = None
+    if rank == 0 and args.only in (None, "qwen35"):
+        q35 = bench_qwen35(dev, args.steps, args.warmup)
     ms = st["ms"]
     if dist is not None:
         t = torch.tensor([ms], device=dev)
@@ -559,6 +618,8 @@ def run_ours(args):
             result["longctx"] = lc
         if kvs:
             result["kvstate"] = kvs
+        if q35:
+            result["qwen35_layer"] = q35
         if vl:
             vl["roofline"] = {"bound": "hbm", "achieved": round(vl["value"] / world, 1),
                               "peak": hbm, "unit": "GB/s",
@@ -647,7 +708,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--only", choices=["decode", "e2e", "prefill", "longctx", "varlen",
-                                       "kvstate"],
+                                       "kvstate", "qwen35"],
                     default=None,
                     help="profiling aid: run the decode timing plus only this extra part")
     ap.add_argument("--batch", type=int, default=WL["B"],

@@ -209,6 +209,45 @@ int b2a_imrope_append(const float* q, long long q_tok_stride, const float* k,
 int b2a_kv_convert(const void* src, int src_dtype, void* dst, int dst_dtype, long long n,
                    void* stream);
 
+/* Qwen35 full-attention prologue for n_tok tokens (the part of
+ * Qwen35Model._attention between the projections and the attention read,
+ * alpaccaroo/qwen35_runtime.py:606-646; device kernels split_query_gate,
+ * rms_norm, imrope, kv_append of qwen35_cuda.py:907-1008, wired in
+ * qwen35_cuda_graph.py:781-829).  For each token and head:
+ *   q_h = IMROPE(RMSNorm(query part of query_gate row h, q_norm))  -> q_out
+ *   k_g = IMROPE(RMSNorm(key row g, k_norm))  -> k_cache row pos (head g)
+ *   v_g                                       -> v_cache row pos (head g)
+ * RMSNorm is x / sqrt(mean(x^2) + epsilon) * w, evaluated in double relative
+ * to max(|x|, sqrt(epsilon)) and rounded to f32 (qwen35_ops.py:46-75);
+ * IMROPE is b2a_imrope_append's rotation (pairs (j, j+P), P = sum(sections)).
+ *
+ *   query_gate f32 [n_tok] rows of [H][ query(D) | gate(D) ], qg_tok_stride apart
+ *   key, value f32 [n_tok] rows of [KV][D]
+ *   q_norm, k_norm f32 [D]
+ *   lanes_dev  int32 [n_tok][4] position lanes ([p,p,p,0] for text)
+ *   pos_dev    int32 [n_tok]    cache row of each token
+ *   q_out      [n_tok][H][D] of q_out_dtype
+ * Caches and tok_seq_mode as in b2a_rope_append.  D even, <= 256; H a
+ * multiple of KV.  The gates stay in query_gate for b2a_sigmoid_gate. */
+int b2a_qwen35_attn_prep(const float* query_gate, long long qg_tok_stride, const float* key,
+                         long long k_tok_stride, const float* value, long long v_tok_stride,
+                         const float* q_norm, const float* k_norm, double epsilon,
+                         const int* lanes_dev, const int* sections, double freq_base,
+                         double freq_scale, const int* pos_dev, int tok_seq_mode, void* k_cache,
+                         void* v_cache, long long seq_stride, int n_ctx, int kv_dtype,
+                         void* q_out, int q_out_dtype, int n_tok, int H, int KV, int D,
+                         void* stream);
+
+/* out[r][c] = values[r][c] * sigmoid(gates[r][c]) for rows x width f32
+ * elements, each array with its own row stride (elements); evaluated in
+ * double and rounded to f32 (the attention output gate of
+ * qwen35_runtime.py:652-659 with tensor.py:123-129's stable sigmoid; device
+ * kernel sigmoid_gate, qwen35_cuda.py:953-963).  For a Qwen35 layer the gates
+ * are read in place: gates = query_gate + D, gate_row_stride = 2*D. */
+int b2a_sigmoid_gate(const float* values, long long value_row_stride, const float* gates,
+                     long long gate_row_stride, float* out, long long out_row_stride, int rows,
+                     int width, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -35,3 +35,7 @@ from .rope import (  # noqa: F401
     imrope_rotate,
     imrope_append,
 )
+from .qwen35_layer import (  # noqa: F401
+    qwen35_rms_norm,
+    qwen35_attention_layer,
+)

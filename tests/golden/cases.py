@@ -121,3 +121,23 @@ def kv_state_case():
     v = rng.standard_normal((L, KV, D), dtype=np.float32)
     return dict(layer_index=3, L=L, KV=KV, D=D, truncate=20, k=k, v=v, sha256=_digest(k, v))
 
+
+def qwen35_layer_case():
+    """The device half of one Qwen35 full-attention layer for one token:
+    4 query / 2 KV heads, key = value length 64, IMROPE sections (8, 8, 8, 0)
+    (48 rotated dims of 64), base 1e7, RMS epsilon 1e-6; 40 earlier rows
+    in the cache, the new token at position 40.  Inputs are the projected
+    query|gate rows, key and value rows and the q/k norm weights."""
+    rng = np.random.default_rng(33)
+    H, KV, D, L = 4, 2, 64, 40
+    qg = rng.standard_normal(H * 2 * D, dtype=np.float32)
+    k = rng.standard_normal(KV * D, dtype=np.float32)
+    v = rng.standard_normal(KV * D, dtype=np.float32)
+    qn = (1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    kn = (1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    k_prev = rng.standard_normal((L, KV, D), dtype=np.float32)
+    v_prev = rng.standard_normal((L, KV, D), dtype=np.float32)
+    return dict(H=H, KV=KV, D=D, L=L, sections=(8, 8, 8, 0), base=1e7, eps=1e-6,
+                query_gate=qg, key=k, value=v, q_norm=qn, k_norm=kn, k_prev=k_prev,
+                v_prev=v_prev, sha256=_digest(qg, k, v, qn, kn, k_prev, v_prev))
+

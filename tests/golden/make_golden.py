@@ -125,9 +125,55 @@ def make_kv_state():
         length_cut=cut.logical_length, memory_bytes_cut=cut.memory_bytes())
 
 
+def make_qwen35_layer():
+    """The reference's Qwen35 full-attention layer (alpaccaroo/qwen35_runtime.py:
+    597-664) run on preset projections: a stub supplies _matvec (the projected
+    rows, and the identity for the output projection) and the layer's own
+    trace boundaries are recorded."""
+    import types
+    from alpaccaroo import memory, qwen35_runtime  # noqa: WPS433
+    c = cases.qwen35_layer_case()
+    cfg = types.SimpleNamespace(query_heads=c["H"], kv_heads=c["KV"], key_length=c["D"],
+                                value_length=c["D"], rms_epsilon=c["eps"],
+                                rope_freq_base=c["base"],
+                                rope_dimension_sections=c["sections"])
+    out_proj = object()
+
+    class Stub:
+        config = cfg
+
+        def _matvec(self, matrix, values):
+            return values if matrix is out_proj else matrix
+
+        def _attention_read(self, query_heads, state):
+            return qwen35_runtime._causal_gqa_one(query_heads, state)
+
+    w = types.SimpleNamespace(query_gate=c["query_gate"].tolist(), key=c["key"].tolist(),
+                              value=c["value"].tolist(), query_norm=c["q_norm"].tolist(),
+                              key_norm=c["k_norm"].tolist(), output=out_proj)
+    spec = memory.LayerMemorySpec(layer_index=0, kind="attention", kv_heads=c["KV"],
+                                  key_dim=c["D"], value_dim=c["D"])
+    st = memory.FullAttentionState(spec)
+    for p in range(c["L"]):
+        st.append(c["k_prev"][p].ravel().tolist(), c["v_prev"][p].ravel().tolist())
+    seen = {}
+
+    def trace(name, values):
+        seen[name.split(".", 2)[-1]] = np.asarray(values, dtype=np.float32).copy()
+
+    qwen35_runtime.Qwen35Model._attention(Stub(), 0, w, [], st, c["L"], trace)
+    np.savez_compressed(
+        os.path.join(HERE, "qwen35_layer.npz"), input_sha256=c["sha256"],
+        q_normed=seen["Qcur_normed"], k_normed=seen["Kcur_normed"],
+        pregate=seen["attn_pregate"], gated=seen["attn_gated"],
+        appended_key=np.frombuffer(bytes(st.key), np.float32)[-c["KV"] * c["D"]:],
+        appended_value=np.frombuffer(bytes(st.value), np.float32)[-c["KV"] * c["D"]:])
+
+
 def main():
     model_mod, qk_mod, ops_mod = _import_reference()
     make_kv_state()
+    make_qwen35_layer()
     make_decode_config1(model_mod)
     make_rope_neox(model_mod)
     make_prefill(model_mod)

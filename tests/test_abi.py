@@ -129,3 +129,20 @@ def test_kv_convert_rejects_bad_arguments(lib):
     assert lib.b2a_kv_convert(p, 7, q, _lib.F32, 8, None) == _lib.ERR_DTYPE
     assert lib.b2a_kv_convert(p, _lib.F16, q, 7, 8, None) == _lib.ERR_DTYPE
     assert lib.b2a_kv_convert(p, _lib.F32, p + 16, _lib.F16, 8, None) == _lib.ERR_ARG  # overlap
+
+
+def test_qwen35_layer_entries_reject_bad_arguments(lib):
+    p = 1 << 20
+    sec = (ctypes.c_int * 4)(8, 8, 8, 0)
+    args = [p, 512, p, 128, p, 128, p, p, 1e-6, p, sec, 1e7, 1.0, p, 1, p, p, 64 * 128, 64,
+            _lib.F32, p, _lib.F32, 0, 4, 2, 64, None]
+    assert lib.b2a_qwen35_attn_prep(*args) == _lib.OK  # n_tok = 0: checks only
+    bad = list(args); bad[8] = 0.0  # epsilon
+    assert lib.b2a_qwen35_attn_prep(*bad) == _lib.ERR_ARG
+    bad = list(args); bad[23] = 3  # H not a multiple of KV
+    assert lib.b2a_qwen35_attn_prep(*bad) == _lib.ERR_SHAPE
+    bad = list(args); bad[25] = 40  # 2 * sum(sections) > D
+    assert lib.b2a_qwen35_attn_prep(*bad) == _lib.ERR_SHAPE
+    assert lib.b2a_sigmoid_gate(p, 64, p, 128, p, 64, 0, 64, None) == _lib.OK
+    assert lib.b2a_sigmoid_gate(None, 64, p, 128, p, 64, 4, 64, None) == _lib.ERR_ARG
+    assert lib.b2a_sigmoid_gate(p, 32, p, 128, p, 64, 4, 64, None) == _lib.ERR_SHAPE

@@ -121,3 +121,19 @@ def test_lse_combine_of_shards_equals_full():
     out2, _ = oracle.lse_combine(np.concatenate([np.stack(os_), np.zeros((1, H, D))]),
                                  np.concatenate([np.stack(ls_), np.full((1, H), -np.inf)]))
     assert rel_err(out2, out) < 1e-12
+
+
+def test_qwen35_layer_matches_reference(golden):
+    g = golden("qwen35_layer.npz")
+    c = cases.qwen35_layer_case()
+    assert c["sha256"] == str(g["input_sha256"])
+    q, k, att, gated = oracle.qwen35_attention_layer(
+        c["query_gate"], c["key"], c["value"], c["q_norm"], c["k_norm"], c["eps"],
+        c["sections"], c["base"], c["L"], c["k_prev"], c["v_prev"])
+    # same double-precision steps rounded to f32 at the same boundaries: bit-exact
+    assert np.array_equal(q.ravel(), g["q_normed"])
+    assert np.array_equal(k.ravel(), g["k_normed"])
+    assert np.array_equal(k.ravel(), g["appended_key"])
+    assert np.array_equal(c["value"], g["appended_value"])
+    assert np.array_equal(att.ravel(), g["pregate"])
+    assert np.array_equal(gated.ravel(), g["gated"])
