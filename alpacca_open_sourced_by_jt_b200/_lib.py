@@ -77,6 +77,9 @@ SIGNATURES = [
                                      c_int, c_int, c_int, c_int, c_int, c_void_p]),
     ("b2a_sigmoid_gate", c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_void_p,
                                  c_longlong, c_int, c_int, c_void_p]),
+    ("b2a_q8_gemv", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int,
+                            c_float, c_void_p, c_int, c_void_p]),
+    ("b2a_q8_embed", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
 ]
 
 _lib = None

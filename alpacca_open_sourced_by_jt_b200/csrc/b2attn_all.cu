@@ -8,3 +8,4 @@
 #include "prefill_head.cu"
 #include "kvconvert.cu"
 #include "qwen35_layer.cu"
+#include "q8gemv.cu"

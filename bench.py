@@ -21,6 +21,8 @@ Also reported on the same line:
             layer (HBM GB/s) and a whole-layer f32 snapshot
   qwen35_layer  Qwen35 full-attention layer step (prologue, decode, gate) at
             16 x 32K rows, 16/2 heads, head_dim 256, bf16, GB/s
+  decode_step  BASELINE config 5: a whole decode token of a 16-layer Q8_0
+            llama decoder as one CUDA graph, tokens/s (device and e2e)
   e2e       the decode step through the public API with host buffers
             (DecodeStep, one CUDA graph per token): per step the pinned host
             q/k/v rows and positions go H2D, the fused RoPE+append writes
@@ -427,6 +429,76 @@ def bench_qwen35(dev, steps, warmup):
                       "for lanes and lengths)"}
 
 
+C5 = dict(n_layer=16, n_embd=2048, n_head=32, n_kv=8, head_dim=64, n_ff=8192, n_vocab=128256,
+          rms_eps=1e-5, rope_base=500000.0)
+
+
+def bench_decode_step(dev, steps, warmup):
+    """a whole decode token of a random-init 16-layer
+    llama decoder (hidden 2048, 32/8 heads of 64, FFN 8192 SwiGLU, vocab
+    128256, RMSNorm 1e-5) with Q8_0 weights N(0, 0.02) (seed 5), an fp16 KV
+    cache holding a full 4096-row context, batch 1, the token replayed as one
+    CUDA graph (decode_chain.DecodeChain).  value: tokens/s from CUDA events
+    over back-to-back graph replays; e2e: tokens/s of chain(token, pos), the
+    public call (token/position H2D, logits D2H, host waits each token).
+    Bytes per token: the Q8_0 weights read (1.0625 B/weight, one embedding
+    row) plus the KV rows attended."""
+    import torch
+    from alpacca_open_sourced_by_jt_b200.decode_chain import DecodeChain, LlamaQ8
+    n_ctx = 4096
+    m = LlamaQ8.random(**C5, seed=5, dev=dev)
+    chain = DecodeChain(m, n_ctx, torch.float16)
+    g = torch.Generator(device=dev).manual_seed(6)
+    for k, v in zip(chain.k_cache, chain.v_cache):
+        k.normal_(generator=g)
+        v.normal_(generator=g)
+    token, pos = 1234, n_ctx - 1
+    chain._h_i_np[:] = (token, pos, pos + 1)
+    for _ in range(max(warmup, 3)):
+        chain._graph.replay()
+    n = max(10, min(steps, 500))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(n):
+        chain._graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    for _ in range(3):
+        chain(token, pos)
+    t0 = time.perf_counter()
+    for _ in range(n):
+        chain(token, pos)
+    ms_e2e = (time.perf_counter() - t0) / n * 1e3
+    kv_bytes = C5["n_layer"] * 2 * n_ctx * C5["n_kv"] * C5["head_dim"] * 2
+    per_tok = m.weight_bytes() + kv_bytes
+    gbs = per_tok / (ms * 1e-3) / 1e9
+    hbm, _, _, src = peaks()
+    _lib_err = None
+    try:
+        from alpacca_open_sourced_by_jt_b200 import _lib
+        _lib.raise_device_error()
+    except Exception as e:  # surfaced in the JSON rather than lost
+        _lib_err = str(e)
+    res = {"metric": "config 5 decode tokens/s (whole token, one CUDA graph)",
+           "value": round(1e3 / ms, 1), "unit": "tokens/s", "ms_per_token": round(ms, 4),
+           "gbs": round(gbs, 1), "bytes_per_token": int(per_tok), "steps": n,
+           "gpu_launches_per_token": chain.launches,
+           "e2e": {"value": round(1e3 / ms_e2e, 1), "unit": "tokens/s",
+                   "ms_per_token": round(ms_e2e, 4), "h2d_bytes_per_step": 12,
+                   "d2h_bytes_per_step": C5["n_vocab"] * 4},
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(gbs / hbm, 4),
+                        "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)"},
+           "config": "16 layers, hidden 2048, 32/8 heads x 64, FFN 8192, vocab 128256, Q8_0 "
+                     "N(0,0.02) seed 5, fp16 KV 4096 rows, batch 1; weights 1.31 GB > L2"}
+    if _lib_err:
+        res["device_error"] = _lib_err
+    del chain, m
+    return res
+
+
 def bench_e2e(dev, st, steps, warmup):
     """Decode step through the public API with host buffers (see module doc):
     DecodeStep replays the whole step (H2D of the pinned rows, fused
@@ -571,6 +643,9 @@ def run_ours(args):
     q35 = None
     if rank == 0 and args.only in (None, "qwen35"):
         q35 = bench_qwen35(dev, args.steps, args.warmup)
+    c5 = None
+    if rank == 0 and args.only in (None, "decode_step"):
+        c5 = bench_decode_step(dev, args.steps, args.warmup)
     ms = st["ms"]
     if dist is not None:
         t = torch.tensor([ms], device=dev)
@@ -620,6 +695,8 @@ def run_ours(args):
             result["kvstate"] = kvs
         if q35:
             result["qwen35_layer"] = q35
+        if c5:
+            result["decode_step"] = c5
         if vl:
             vl["roofline"] = {"bound": "hbm", "achieved": round(vl["value"] / world, 1),
                               "peak": hbm, "unit": "GB/s",
@@ -708,7 +785,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--only", choices=["decode", "e2e", "prefill", "longctx", "varlen",
-                                       "kvstate", "qwen35"],
+                                       "kvstate", "qwen35", "decode_step"],
                     default=None,
                     help="profiling aid: run the decode timing plus only this extra part")
     ap.add_argument("--batch", type=int, default=WL["B"],

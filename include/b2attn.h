@@ -248,6 +248,38 @@ int b2a_sigmoid_gate(const float* values, long long value_row_stride, const floa
                      long long gate_row_stride, float* out, long long out_row_stride, int rows,
                      int width, void* stream);
 
+/* b2a_q8_gemv flags */
+#define B2A_GEMV_ACCUMULATE 1 /* out[r] += product (the residual stream) */
+#define B2A_GEMV_SWIGLU_OUT 2 /* rows interleave gate/up: out[i] = silu(row 2i) * row 2i+1 */
+#define B2A_GEMV_PDL 4        /* launch as a programmatic dependent of the previous kernel */
+
+/* Q8_0 matrix-vector product for a decode step (batch 1):
+ *   out[r] (=|+=) sum_b d[r][b] * sum_{l<32} q[r][32b+l] * xin[32b+l]
+ * the reference's Q8_0 matvec (alpaccaroo/qmatrix.py:312-320, device chain
+ * kernel cuda.py:241-286), with the step's input transform fused:
+ *   mode 0  xin = x                                        (x: cols f32)
+ *   mode 1  xin = x * (1/sqrt(x.x/cols + eps)) * aux       (RMSNorm,
+ *           tensor.py:349-356; aux = the norm weight)
+ *   mode 2  xin = g / (1 + exp(-g)) * u, g = x[0:cols], u = x[cols:2cols]
+ *           (SwiGLU, model.py:1466-1467)
+ flags: B2A_GEMV_ACCUMULATE adds into out (the residual stream);
+ * B2A_GEMV_SWIGLU_OUT, for a matrix whose rows interleave the FFN's gate and
+ * up rows, writes out[i] = g/(1+exp(-g))*u of the row pair (rows/2 values);
+ * B2A_GEMV_PDL launches the kernel as a programmatic dependent of the
+ * previous kernel on the stream: it prefetches its weights into L2 while
+ * that kernel finishes and reads x only after it completed.  Weights are the
+ * Q8_0 records repacked: codes int8 [rows][cols] (16-byte aligned rows),
+ * scales f16 [rows][cols/32].  cols a multiple of 32, <= 16384; codes, x
+ * and aux 16-byte aligned. */
+int b2a_q8_gemv(const void* codes, const void* scales, int rows, int cols, const float* x,
+                const float* aux, int mode, float eps, float* out, int flags, void* stream);
+
+/* out[c] = q[token][c] * d[token][c/32] (token read from token_dev): one
+ * dequantized Q8_0 embedding row (qmatrix.py:445-447; T.matrix_row at
+ * model.py:1396).  A token outside [0, rows) records B2A_ERR_POSITION. */
+int b2a_q8_embed(const void* codes, const void* scales, int rows, int cols, const int* token_dev,
+                 float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

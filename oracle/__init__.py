@@ -39,3 +39,4 @@ from .qwen35_layer import (  # noqa: F401
     qwen35_rms_norm,
     qwen35_attention_layer,
 )
+from . import llama_q8  # noqa: F401

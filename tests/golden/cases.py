@@ -141,3 +141,39 @@ def qwen35_layer_case():
                 query_gate=qg, key=k, value=v, q_norm=qn, k_norm=kn, k_prev=k_prev,
                 v_prev=v_prev, sha256=_digest(qg, k, v, qn, kn, k_prev, v_prev))
 
+
+def llama_q8_case():
+    """A small llama-architecture model with Q8_0 weights N(0, 0.02) (seed 5),
+    quantized by the reference's Q8_0 rule (oracle.llama_q8.quantize_q8_0):
+    2 layers, hidden 256, 4 q / 2 KV heads of 64, FFN 512, vocab 1024,
+    RMSNorm eps 1e-5, RoPE base 5e5 (norm style); six decode tokens."""
+    from oracle.llama_q8 import quantize_q8_0
+    rng = np.random.default_rng(5)
+    E, H, KV, D, F, V = 256, 4, 2, 64, 512, 1024
+
+    def mat(rows, cols):
+        return quantize_q8_0(rng.normal(0.0, 0.02, (rows, cols)).astype(np.float32))
+
+    def norm(n):
+        return (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+
+    layers = []
+    for _ in range(2):
+        layers.append(dict(attn_norm=norm(E), wq=mat(H * D, E), wk=mat(KV * D, E),
+                           wv=mat(KV * D, E), wo=mat(E, H * D), ffn_norm=norm(E),
+                           w_gate=mat(F, E), w_up=mat(F, E), w_down=mat(E, F)))
+    tok_embd = mat(V, E)
+    out_norm = norm(E)
+    output = mat(V, E)
+    blobs = [tok_embd, output, out_norm.tobytes()] + [
+        (ly[k] if isinstance(ly[k], bytes) else ly[k].tobytes())
+        for ly in layers for k in sorted(ly)]
+    import hashlib
+    h = hashlib.sha256()
+    for b in blobs:
+        h.update(b)
+    return dict(n_layer=2, n_embd=E, n_head=H, n_kv=KV, head_dim=D, n_ff=F, n_vocab=V,
+                rms_eps=1e-5, rope_base=500000.0, n_ctx=32, layers=layers,
+                tok_embd=tok_embd, out_norm=out_norm, output=output,
+                tokens=[1, 5, 17, 300, 1023, 42], sha256=h.hexdigest())
+

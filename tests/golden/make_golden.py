@@ -170,9 +170,49 @@ def make_qwen35_layer():
         appended_value=np.frombuffer(bytes(st.value), np.float32)[-c["KV"] * c["D"]:])
 
 
+def make_llama_q8(model_mod):
+    """The reference's own decode step (Model._forward_np, model.py:1374-1487)
+    on a small Q8_0 llama model built in memory; the oracle's Q8_0 encoder is
+    checked byte for byte against the reference's quantize_q8_0 first."""
+    from alpaccaroo import quants  # noqa: WPS433
+    from alpaccaroo.qmatrix import QuantMatrix  # noqa: WPS433
+    c = cases.llama_q8_case()
+    rng = np.random.default_rng(99)
+    probe = rng.normal(0.0, 0.02, 32 * 64).astype(np.float32)
+    from oracle.llama_q8 import quantize_q8_0
+    assert quants.quantize_q8_0(probe.tolist()) == quantize_q8_0(probe)
+    E, H, KV, D, F, V = (c["n_embd"], c["n_head"], c["n_kv"], c["head_dim"], c["n_ff"],
+                         c["n_vocab"])
+    hp = model_mod.Hyperparams(arch="llama", n_layer=c["n_layer"], n_embd=E, n_head=H,
+                               n_kv=KV, n_ff=F, n_vocab=V, n_ctx_train=4096, head_dim=D,
+                               n_rot=D, rms_eps=c["rms_eps"], rope_base=c["rope_base"],
+                               rope_style="norm")
+    m = model_mod.Model(hp, None)
+    m.n_ctx = c["n_ctx"]
+    qm = lambda data, rows, cols: QuantMatrix(data, "Q8_0", rows, cols)  # noqa: E731
+    for cl in c["layers"]:
+        ly = model_mod.Layer()
+        for slot in model_mod.Layer.__slots__:
+            setattr(ly, slot, None)
+        ly.attn_norm, ly.ffn_norm = cl["attn_norm"], cl["ffn_norm"]
+        ly.wq, ly.wk, ly.wv = qm(cl["wq"], H * D, E), qm(cl["wk"], KV * D, E), qm(cl["wv"], KV * D, E)
+        ly.wo = qm(cl["wo"], E, H * D)
+        ly.w_gate, ly.w_up, ly.w_down = qm(cl["w_gate"], F, E), qm(cl["w_up"], F, E), \
+            qm(cl["w_down"], E, F)
+        m.layers.append(ly)
+    m.tok_embd = qm(c["tok_embd"], V, E)
+    m.out_norm = c["out_norm"]
+    m.output = qm(c["output"], V, E)
+    m._init_cache()
+    logits = np.stack([np.asarray(m._forward_np(t), dtype=np.float32) for t in c["tokens"]])
+    np.savez_compressed(os.path.join(HERE, "llama_q8.npz"), weights_sha256=c["sha256"],
+                        tokens=np.array(c["tokens"], np.int32), logits=logits)
+
+
 def main():
     model_mod, qk_mod, ops_mod = _import_reference()
     make_kv_state()
+    make_llama_q8(model_mod)
     make_qwen35_layer()
     make_decode_config1(model_mod)
     make_rope_neox(model_mod)

@@ -137,3 +137,17 @@ def test_qwen35_layer_matches_reference(golden):
     assert np.array_equal(c["value"], g["appended_value"])
     assert np.array_equal(att.ravel(), g["pregate"])
     assert np.array_equal(gated.ravel(), g["gated"])
+
+
+def test_llama_q8_decode_matches_reference(golden):
+    g = golden("llama_q8.npz")
+    c = cases.llama_q8_case()
+    assert c["sha256"] == str(g["weights_sha256"])
+    n_ctx, KV, D = c["n_ctx"], c["n_kv"], c["head_dim"]
+    cos, sin = oracle.rope_tables(n_ctx, D, c["rope_base"])
+    ck = [np.zeros((n_ctx, KV, D), np.float32) for _ in range(c["n_layer"])]
+    cv = [np.zeros((n_ctx, KV, D), np.float32) for _ in range(c["n_layer"])]
+    for pos, tok in enumerate(c["tokens"]):
+        logits = oracle.llama_q8.forward_token(c, tok, pos, ck, cv, cos, sin)
+        # same f32 operations; BLAS/einsum reduction orders differ from NumPy's here
+        assert rel_err(logits, g["logits"][pos]) < 1e-5
