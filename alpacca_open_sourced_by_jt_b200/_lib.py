@@ -79,7 +79,12 @@ SIGNATURES = [
                                  c_longlong, c_int, c_int, c_void_p]),
     ("b2a_q8_gemv", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int,
                             c_float, c_void_p, c_int, c_void_p]),
-    ("b2a_q8_embed", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    ("b2a_q8_embed", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p,
+                             c_void_p]),
+    ("b2a_rmsnorm_rows", c_int, [c_void_p, c_longlong, c_void_p, c_float, c_void_p, c_longlong,
+                                 c_int, c_int, c_int, c_void_p]),
+    ("b2a_swiglu_rows", c_int, [c_void_p, c_longlong, c_int, c_void_p, c_longlong, c_int, c_int,
+                                c_int, c_void_p]),
 ]
 
 _lib = None

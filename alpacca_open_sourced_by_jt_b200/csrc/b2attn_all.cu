@@ -9,3 +9,4 @@
 #include "kvconvert.cu"
 #include "qwen35_layer.cu"
 #include "q8gemv.cu"
+#include "rowops.cu"

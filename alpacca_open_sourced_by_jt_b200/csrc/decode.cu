@@ -64,6 +64,9 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
     const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
     const float* __restrict__ q, const int* __restrict__ lens, float* __restrict__ part_o,
     float* __restrict__ part_ml, int H, int group, int split_rows, int n_splits, float qscale) {
+  // a programmatic dependent launched after this kernel may start its
+  // independent prologue now (it waits for this kernel before reading)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   using C = Cfg<D>;
   constexpr int KS = D / 16;  // k-steps of QK^T, m-tiles of PV
   extern __shared__ uint8_t smem_raw[];
@@ -426,6 +429,9 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(
     const float* __restrict__ part_o, const float* __restrict__ part_ml,
     const int* __restrict__ lens, float* __restrict__ out, float* __restrict__ lse, int H, int D,
     int split_rows, int n_splits, int row_limit) {
+  // a programmatic dependent launched after this kernel may start its
+  // independent prologue now (it waits for this kernel before reading)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ float wsm[];  // [n_splits] weights
   __shared__ float red[kCombineThreads / 32];
   __shared__ float s_M, s_invL;

@@ -24,7 +24,8 @@
 // 2i+1 = up_i), write the SwiGLU of each row pair (the FFN's activation).
 //
 // Each warp walks its rows as slabs (a row pair x 64 blocks) with the next
-// slab's loads in flight while it computes the current one.  Chained
+// slab's loads in flight while it computes the current one; rows longer
+// than 2048 columns are split across the warps of a CTA.  Chained
 // launches (flag B2A_GEMV_PDL) use programmatic dependent launch: every CTA
 // lets the next kernel launch at once and issues its first slab's loads
 // (the weights do not depend on the previous kernel) before it waits for
@@ -75,29 +76,39 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(
 
   // Work unit: a slab = one row pair x 64 blocks (lane l: blocks
   // part*64 + l and part*64 + 32 + l of both rows, 128 bytes of codes).  A
-  // row pair has ceil(nb/64) slabs; each warp walks its pairs' slabs with
-  // the next slab's loads in flight while it computes the current one.
+  // row pair has spp = ceil(nb/64) slabs, taken by spp warps of the same CTA
+  // (a long row is split across warps, their sums meet in shared memory),
+  // so a CTA round covers ppr = kWarps / spp pairs.  Each warp walks its
+  // rounds with the next round's slab loads in flight while it computes the
+  // current one.
   const int spp = (nb + 63) >> 6;
+  const int ppr = kWarps / spp;
+  const int wpair = warp / spp, wpart = warp % spp;
+  const bool wactive = wpair < ppr;
   const int pairs = (rows + kRows - 1) / kRows;
-  const int wstride = gridDim.x * kWarps;
-  const int first = blockIdx.x * kWarps + warp;
-  const int my_pairs = first < pairs ? (pairs - 1 - first) / wstride + 1 : 0;
-  const int n_slabs = my_pairs * spp;
+  const int groups = (pairs + ppr - 1) / ppr;
+  const int n_rounds = static_cast<int>(blockIdx.x) < groups
+                           ? (groups - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1
+                           : 0;
+  __shared__ float psum[2][kWarps][kRows];  // per round parity
 
   struct Slab {
     uint4 c[kRows][2][2];
     float d[kRows][2];
   };
-  auto load = [&](int i, Slab& sl) {
-    const int pr = first + (i / spp) * wstride, part = i % spp;
+  // pair handled by this warp in round j (>= pairs: none)
+  auto pair_of = [&](int j) { return (blockIdx.x + j * gridDim.x) * ppr + wpair; };
+  auto load = [&](int j, Slab& sl) {
+    const int pr = pair_of(j);
+    const bool live = wactive && pr < pairs;
     const int r0 = pr * kRows;
 #pragma unroll
     for (int r = 0; r < kRows; ++r) {
       const int row = min(r0 + r, rows - 1);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int blk = part * 64 + h * 32 + lane;
-        if (blk < nb) {
+        const int blk = wpart * 64 + h * 32 + lane;
+        if (live && blk < nb) {
           const uint4* p = reinterpret_cast<const uint4*>(codes + static_cast<size_t>(row) * cols +
                                                           blk * 32);
           sl.c[r][h][0] = __ldg(p);
@@ -115,7 +126,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(
   // ---- overlap with the previous kernel: release the next, load weights ---
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   Slab cur, nxt;
-  if (n_slabs > 0) load(0, cur);  // weights do not depend on the previous kernel
+  if (n_rounds > 0) load(0, cur);  // weights do not depend on the previous kernel
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- stage x (with the prologue) ---------------------------------------
@@ -158,14 +169,13 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(
   }
   __syncthreads();
 
-  // ---- slabs ---------------------------------------------------------------
-  float acc[kRows] = {0.f, 0.f};
-  for (int i = 0; i < n_slabs; ++i) {
-    if (i + 1 < n_slabs) load(i + 1, nxt);
-    const int part = i % spp;
+  // ---- rounds --------------------------------------------------------------
+  for (int j = 0; j < n_rounds; ++j) {
+    if (j + 1 < n_rounds) load(j + 1, nxt);
+    float acc[kRows] = {0.f, 0.f};
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const int blk = part * 64 + h * 32 + lane;
+      const int blk = wpart * 64 + h * 32 + lane;
       if (blk < nb) {
 #pragma unroll
         for (int r = 0; r < kRows; ++r)
@@ -173,44 +183,56 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(
                         acc[r]);
       }
     }
-    if (part == spp - 1) {
-      const int r0 = (first + (i / spp) * wstride) * kRows;
-      const bool two = r0 + 1 < rows;
-      float a0 = acc[0], a1 = acc[1];
-      for (int o = 16; o > 0; o >>= 1) {
-        a0 += __shfl_xor_sync(0xffffffffu, a0, o);
-        a1 += __shfl_xor_sync(0xffffffffu, a1, o);
-      }
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+      for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+    if (spp > 1) {
       if (lane == 0) {
-        if (Epi == 1) {
-          out[r0] += a0;
-          if (two) out[r0 + 1] += a1;
-        } else if (Epi == 2) {
-          out[r0 >> 1] = a0 / (1.f + expf(-a0)) * a1;  // gate_i = row 2i, up_i = row 2i+1
-        } else {
-          out[r0] = a0;
-          if (two) out[r0 + 1] = a1;
+        psum[j & 1][warp][0] = acc[0];
+        psum[j & 1][warp][1] = acc[1];
+      }
+      __syncthreads();
+      if (wactive && wpart == 0) {  // the pair's first warp adds its siblings' sums in order
+        for (int t = 1; t < spp; ++t) {
+          acc[0] += psum[j & 1][warp + t][0];
+          acc[1] += psum[j & 1][warp + t][1];
         }
       }
-      acc[0] = acc[1] = 0.f;
     }
-    if (i + 1 < n_slabs) cur = nxt;
+    const int pr = pair_of(j);
+    if (wactive && wpart == 0 && lane == 0 && pr < pairs) {
+      const int r0 = pr * kRows;
+      const bool two = r0 + 1 < rows;
+      const float a0 = acc[0], a1 = acc[1];
+      if (Epi == 1) {
+        out[r0] += a0;
+        if (two) out[r0 + 1] += a1;
+      } else if (Epi == 2) {
+        out[r0 >> 1] = a0 / (1.f + expf(-a0)) * a1;  // gate_i = row 2i, up_i = row 2i+1
+      } else {
+        out[r0] = a0;
+        if (two) out[r0 + 1] = a1;
+      }
+    }
+    if (j + 1 < n_rounds) cur = nxt;
   }
 }
 
-// out[c] = code[token][c] * d[token][c / 32]  (qmatrix.py:445-447)
+// out[i][c] = code[tok_i][c] * d[tok_i][c / 32]  (qmatrix.py:445-447), one
+// grid row (blockIdx.y) per token
 __global__ void embed_kernel(const int8_t* __restrict__ codes, const __half* __restrict__ scales,
-                             int rows, int cols, const int* __restrict__ token,
+                             int rows, int cols, const int* __restrict__ tokens,
                              float* __restrict__ out) {
-  const int t = *token;
+  const int t = tokens[blockIdx.y];
   if (t < 0 || t >= rows) {
     if (threadIdx.x == 0 && blockIdx.x == 0) set_dev_error(B2A_ERR_POSITION, t);
     return;
   }
   const int8_t* row = codes + static_cast<size_t>(t) * cols;
   const __half* sr = scales + static_cast<size_t>(t) * (cols >> 5);
+  float* o = out + static_cast<size_t>(blockIdx.y) * cols;
   for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < cols; c += gridDim.x * blockDim.x)
-    out[c] = static_cast<float>(row[c]) * __half2float(sr[c >> 5]);
+    o[c] = static_cast<float>(row[c]) * __half2float(sr[c >> 5]);
 }
 
 }  // namespace q8
@@ -233,7 +255,8 @@ int launch_gemv(const int8_t* codes, const __half* scales, int rows, int cols, c
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int pairs = (rows + Q::kRows - 1) / Q::kRows;
-  int grid = (pairs + Q::kWarps - 1) / Q::kWarps;
+  const int ppr = Q::kWarps / ((cols / 32 + 63) / 64);  // pairs per CTA round
+  int grid = (pairs + ppr - 1) / ppr;
   int per_sm = 1;  // persistent: at most the resident CTAs, each walks its pairs
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Q::kThreads, smem);
   if (per_sm < 1) per_sm = 1;
@@ -293,18 +316,20 @@ int b2a_q8_gemv(const void* codes, const void* scales, int rows, int cols, const
 #undef B2A_GEMV_CASE
 }
 
-int b2a_q8_embed(const void* codes, const void* scales, int rows, int cols, const int* token_dev,
-                 float* out, void* stream) {
+int b2a_q8_embed(const void* codes, const void* scales, int rows, int cols,
+                 const int* tokens_dev, int n_tok, float* out, void* stream) {
   using b2a_host::fail;
-  if (!codes || !scales || !token_dev || !out)
+  if (!codes || !scales || !tokens_dev || !out)
     return fail(B2A_ERR_ARG, "q8_embed: null pointer argument");
-  if (rows <= 0 || cols <= 0 || (cols & 31)) return fail(B2A_ERR_SHAPE, "q8_embed: bad shape");
+  if (rows <= 0 || cols <= 0 || (cols & 31) || n_tok < 0 || n_tok > 65535)
+    return fail(B2A_ERR_SHAPE, "q8_embed: bad shape");
+  if (n_tok == 0) return B2A_OK;
   const int threads = 256;
   int blocks = (cols + threads - 1) / threads;
   if (blocks > 64) blocks = 64;
-  b2a::q8::embed_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+  b2a::q8::embed_kernel<<<dim3(blocks, n_tok), threads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const int8_t*>(codes), static_cast<const __half*>(scales), rows, cols,
-      token_dev, out);
+      tokens_dev, out);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "q8_embed launch");
   return B2A_OK;

@@ -42,6 +42,9 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(
     const int* __restrict__ pos, int tok_seq_mode, TK* __restrict__ k_cache,
     TK* __restrict__ v_cache, long long seq_stride, int n_ctx, TQ* __restrict__ q_out,
     long long qo_tok_stride, int H, int KV, int D, int n_rot, int neox) {
+  // a programmatic dependent launched after this kernel may start its
+  // independent prologue now (it waits for this kernel before reading)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int i = blockIdx.x;
   const int slot = blockIdx.y;
   const int p = pos[i];

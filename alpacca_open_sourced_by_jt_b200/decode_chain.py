@@ -208,7 +208,7 @@ class DecodeChain:
         st = device._stream(None)
         self._d_i.copy_(self._h_i, non_blocking=True)
         _lib.check(lib.b2a_q8_embed(m.tok_embd.codes.data_ptr(), m.tok_embd.scales.data_ptr(),
-                                    m.V, m.E, self._d_i.data_ptr(), self.x.data_ptr(), st))
+                                    m.V, m.E, self._d_i.data_ptr(), 1, self.x.data_ptr(), st))
         q = self.qkv[:qd].view(1, m.H, m.D)
         k = self.qkv[qd:qd + kd].view(1, m.KV, m.D)
         v = self.qkv[qd + kd:].view(1, m.KV, m.D)

@@ -1,0 +1,123 @@
+"""Device-resident prefill chunks for a Q8_0 llama model.
+
+The reference's batch path (Model.forward_batch, alpaccaroo/model.py:1274-1372;
+its GPU twin DecodeChain.prefill_chunk, cuda.py:1943-2080, with the
+codes-decoding SIMT GEMM of cuda.py:287-422) runs a chunk of T tokens per
+layer as: RMSNorm, q/k/v GEMMs, RoPE with the K/V rows stored at their
+positions, causal GQA attention, output GEMM + residual, RMSNorm, gate/up
+GEMMs, SwiGLU, down GEMM + residual; then the last row's logits.
+
+Here the chunk stays on the device end to end and writes its K/V rows
+straight into a DecodeChain's caches, so decoding continues from it:
+
+  embed rows              b2a_q8_embed (all T tokens)
+  per layer:
+    h    = RMSNorm(x)      b2a_rmsnorm_rows, written as the cache's 16-bit type
+    qkv  = h . Wqkv^T      tensor-core GEMM, f32 out
+    RoPE + K/V append, q rotated to 16 bits           b2a_rope_append
+    att  = causal prefill over cache rows 0..pos0+T-1  b2a_prefill (tcgen05)
+    x   += att . Wo^T      tensor-core GEMM with the residual as its C input
+    h    = RMSNorm(x)      b2a_rmsnorm_rows
+    gu   = h . Wgu^T       (gate/up rows interleaved)
+    act  = SwiGLU(gu)      b2a_swiglu_rows
+    x   += act . Wdown^T
+  logits = Woutput . RMSNorm(x[T-1])   b2a_q8_gemv (the decode path's Q8_0 GEMV)
+
+The GEMMs are plain dense products, so they run through cuBLAS on the
+16-bit dequantized weights (d * code, one copy per matrix made at set-up)
+with f32 accumulation and f32 output; everything fused around them is this
+library's own kernels.  The 16-bit operands are the one precision step away
+from the reference's f32 SIMT GEMM.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _lib, device
+from .decode_chain import DecodeChain, PDL, Q8Matrix
+
+
+def _dequant(q: Q8Matrix, dt: torch.dtype) -> torch.Tensor:
+    """(rows, cols) weights d * code in dt (exact codes, f16 scale, one rounding)."""
+    w = q.codes.float().view(q.rows, q.cols // 32, 32) * q.scales.float()[:, :, None]
+    return w.reshape(q.rows, q.cols).to(dt).contiguous()
+
+
+class ChunkPrefill:
+    """Prefill chunks of up to max_chunk tokens into `chain`'s caches (which
+    must be f16 or bf16: the attention runs on the tcgen05 prefill kernel)."""
+
+    def __init__(self, chain: DecodeChain, max_chunk: int = 256):
+        _lib.load()
+        m = chain.m
+        self.chain, self.m = chain, m
+        dt = chain.k_cache[0].dtype
+        if dt not in (torch.float16, torch.bfloat16):
+            raise _lib.B2AShapeError(_lib.ERR_DTYPE, "chunk prefill needs an f16 or bf16 cache")
+        self.dt, self.code = dt, device._code(dt)
+        dev = m.device
+        self.max_chunk = int(max_chunk)
+        self.w = [dict(qkv=_dequant(ly["wqkv"], dt), wo=_dequant(ly["wo"], dt),
+                       gu=_dequant(ly["wgu"], dt), down=_dequant(ly["w_down"], dt))
+                  for ly in m.layers]
+        T, E, H, KV, D, F = self.max_chunk, m.E, m.H, m.KV, m.D, m.F
+        self.x = torch.zeros((T, E), dtype=torch.float32, device=dev)
+        self.h = torch.zeros((T, E), dtype=dt, device=dev)
+        self.qrot = torch.zeros((T, H, D), dtype=dt, device=dev)
+        self.att = torch.zeros((T, H, D), dtype=dt, device=dev)
+        self.act = torch.zeros((T, F), dtype=dt, device=dev)
+        self.tokens = torch.zeros(T, dtype=torch.int32, device=dev)
+        self.positions = torch.zeros(T, dtype=torch.int32, device=dev)
+        self.logits = torch.zeros(m.V, dtype=torch.float32, device=dev)
+
+    def _norm(self, x, w, T):
+        m = self.m
+        _lib.check(_lib.load().b2a_rmsnorm_rows(
+            x.data_ptr(), m.E, w.data_ptr(), m.eps, self.h.data_ptr(), m.E, self.code, T, m.E,
+            device._stream(None)))
+        return self.h[:T]
+
+    def __call__(self, tokens, pos0: int, want_logits: bool = True):
+        """Run tokens (a list of ids) at cache rows pos0.. and return the last
+        row's logits (a host f32 array) or None."""
+        m, ch = self.m, self.chain
+        T = len(tokens)
+        if not 0 < T <= self.max_chunk:
+            raise _lib.B2AShapeError(_lib.ERR_SHAPE, f"chunk of {T} tokens (max {self.max_chunk})")
+        if pos0 < 0 or pos0 + T > ch.n_ctx:
+            raise _lib.B2AError(_lib.ERR_POSITION, f"rows [{pos0}, {pos0 + T}) outside the cache")
+        toks = np.asarray(tokens, dtype=np.int32)
+        if toks.min() < 0 or toks.max() >= m.V:
+            raise _lib.B2AError(_lib.ERR_ARG, "token id outside the vocabulary")
+        H, KV, D, E = m.H, m.KV, m.D, m.E
+        qd, kd = H * D, KV * D
+        lib = _lib.load()
+        st = device._stream(None)
+        self.tokens[:T].copy_(torch.from_numpy(toks))
+        torch.arange(pos0, pos0 + T, dtype=torch.int32, out=self.positions[:T])
+        pos = self.positions[:T]
+        x = self.x[:T]
+        _lib.check(lib.b2a_q8_embed(m.tok_embd.codes.data_ptr(), m.tok_embd.scales.data_ptr(),
+                                    m.V, E, self.tokens.data_ptr(), T, x.data_ptr(), st))
+        t_kv = pos0 + T
+        for li, (ly, w) in enumerate(zip(m.layers, self.w)):
+            h = self._norm(x, ly["attn_norm"], T)
+            qkv = torch.mm(h, w["qkv"].t(), out_dtype=torch.float32)
+            q = qkv[:, :qd].view(T, H, D)
+            k = qkv[:, qd:qd + kd].view(T, KV, D)
+            v = qkv[:, qd + kd:].view(T, KV, D)
+            device.rope_append(q, k, v, pos, ch.cos, ch.sin, k_cache=ch.k_cache[li],
+                               v_cache=ch.v_cache[li], q_out=self.qrot[:T])
+            att = device.prefill(self.qrot[:T], ch.k_cache[li][0, :t_kv],
+                                 ch.v_cache[li][0, :t_kv], pos, out=self.att[:T])
+            x.copy_(torch.addmm(x, att.view(T, qd), w["wo"].t(), out_dtype=torch.float32))
+            h = self._norm(x, ly["ffn_norm"], T)
+            gu = torch.mm(h, w["gu"].t(), out_dtype=torch.float32)
+            _lib.check(lib.b2a_swiglu_rows(gu.data_ptr(), 2 * m.F, 1, self.act.data_ptr(), m.F,
+                                           self.code, T, m.F, st))
+            x.copy_(torch.addmm(x, self.act[:T], w["down"].t(), out_dtype=torch.float32))
+        if not want_logits:
+            return None
+        m.output.gemv(x[T - 1], self.logits, mode=1, aux=m.out_norm, eps=m.eps, flags=PDL)
+        return self.logits.cpu().numpy()

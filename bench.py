@@ -23,6 +23,8 @@ Also reported on the same line:
             16 x 32K rows, 16/2 heads, head_dim 256, bf16, GB/s
   decode_step  BASELINE config 5: a whole decode token of a 16-layer Q8_0
             llama decoder as one CUDA graph, tokens/s (device and e2e)
+  prefill_chunk  a 2048-token prefill chunk of the same model kept on the
+            device, tokens/s and TFLOP/s
   e2e       the decode step through the public API with host buffers
             (DecodeStep, one CUDA graph per token): per step the pinned host
             q/k/v rows and positions go H2D, the fused RoPE+append writes
@@ -499,6 +501,49 @@ def bench_decode_step(dev, steps, warmup):
     return res
 
 
+def bench_prefill_chunk(dev, steps, warmup):
+    """Device-resident prefill chunk (prefill_chain.ChunkPrefill) on the
+    config-5 model: one 2048-token chunk at position 0 into an fp16 cache of
+    4096 rows.  FLOPs per chunk: the GEMMs (2 * weights * tokens) plus the
+    causal attention (4 * H * D * T(T+1)/2 per layer); bound: tensor cores."""
+    import torch
+    from alpacca_open_sourced_by_jt_b200.decode_chain import DecodeChain, LlamaQ8
+    from alpacca_open_sourced_by_jt_b200.prefill_chain import ChunkPrefill
+    T, n_ctx = 2048, 4096
+    m = LlamaQ8.random(**C5, seed=5, dev=dev)
+    chain = DecodeChain(m, n_ctx, torch.float16)
+    pre = ChunkPrefill(chain, max_chunk=T)
+    toks = [(7 * i + 3) % C5["n_vocab"] for i in range(T)]
+    for _ in range(max(2, min(warmup, 3))):
+        pre(toks, 0, want_logits=False)
+    n = max(3, min(steps, 10))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(n):
+        pre(toks, 0, want_logits=False)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    E, H, KV, D, F, L = (C5["n_embd"], C5["n_head"], C5["n_kv"], C5["head_dim"], C5["n_ff"],
+                         C5["n_layer"])
+    w_layer = E * (H + 2 * KV) * D + H * D * E + 2 * F * E + F * E
+    flops = L * (2.0 * w_layer * T + 4.0 * H * D * T * (T + 1) / 2)
+    tf = flops / (ms * 1e-3) / 1e12
+    _, bf16, _, src = peaks()
+    del pre, chain, m
+    return {"metric": "prefill chunk tokens/s (config-5 model, 2048-token chunk)",
+            "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_chunk": round(ms, 3),
+            "tflops": round(tf, 1), "steps": n,
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": bf16,
+                         "unit": "TFLOP/s", "frac": round(tf / bf16, 4),
+                         "peak_source": f"{src} (MEASURED_PEAKS.json bf16_tflops, burst)"},
+            "config": "16 layers, hidden 2048, 32/8 heads x 64, FFN 8192, vocab 128256; "
+                      "weights dequantized to f16 for the GEMMs (cuBLAS, f32 out), RMSNorm / "
+                      "RoPE+append / tcgen05 causal prefill / SwiGLU kernels of this library; "
+                      "eager launches (about 10 per layer)"}
+
+
 def bench_e2e(dev, st, steps, warmup):
     """Decode step through the public API with host buffers (see module doc):
     DecodeStep replays the whole step (H2D of the pinned rows, fused
@@ -646,6 +691,9 @@ def run_ours(args):
     c5 = None
     if rank == 0 and args.only in (None, "decode_step"):
         c5 = bench_decode_step(dev, args.steps, args.warmup)
+    pch = None
+    if rank == 0 and args.only in (None, "prefill_chunk"):
+        pch = bench_prefill_chunk(dev, args.steps, args.warmup)
     ms = st["ms"]
     if dist is not None:
         t = torch.tensor([ms], device=dev)
@@ -697,6 +745,8 @@ def run_ours(args):
             result["qwen35_layer"] = q35
         if c5:
             result["decode_step"] = c5
+        if pch:
+            result["prefill_chunk"] = pch
         if vl:
             vl["roofline"] = {"bound": "hbm", "achieved": round(vl["value"] / world, 1),
                               "peak": hbm, "unit": "GB/s",
@@ -785,7 +835,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--only", choices=["decode", "e2e", "prefill", "longctx", "varlen",
-                                       "kvstate", "qwen35", "decode_step"],
+                                       "kvstate", "qwen35", "decode_step",
+                                       "prefill_chunk"],
                     default=None,
                     help="profiling aid: run the decode timing plus only this extra part")
     ap.add_argument("--batch", type=int, default=WL["B"],

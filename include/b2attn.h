@@ -274,11 +274,25 @@ int b2a_sigmoid_gate(const float* values, long long value_row_stride, const floa
 int b2a_q8_gemv(const void* codes, const void* scales, int rows, int cols, const float* x,
                 const float* aux, int mode, float eps, float* out, int flags, void* stream);
 
-/* out[c] = q[token][c] * d[token][c/32] (token read from token_dev): one
- * dequantized Q8_0 embedding row (qmatrix.py:445-447; T.matrix_row at
- * model.py:1396).  A token outside [0, rows) records B2A_ERR_POSITION. */
-int b2a_q8_embed(const void* codes, const void* scales, int rows, int cols, const int* token_dev,
-                 float* out, void* stream);
+/* out[i][c] = q[tok_i][c] * d[tok_i][c/32] for the n_tok tokens read from
+ * tokens_dev: dequantized Q8_0 embedding rows (qmatrix.py:445-447;
+ * T.matrix_row / matrix_rows at model.py:1396, :1308).  A token outside
+ * [0, rows) records B2A_ERR_POSITION. */
+int b2a_q8_embed(const void* codes, const void* scales, int rows, int cols,
+                 const int* tokens_dev, int n_tok, float* out, void* stream);
+
+/* Row-wise glue of a device-resident prefill chunk (Model.forward_batch,
+ * model.py:1274-1372; device prefill_chunk, cuda.py:1943-2080):
+ *   b2a_rmsnorm_rows  out[t] = x[t] * (1/sqrt(mean(x[t]^2) + eps)) * w
+ *                     (tensor.py:355-356), out in out_dtype (the GEMM input)
+ *   b2a_swiglu_rows   out[t][i] = g/(1+exp(-g))*u (model.py:1352-1354) with
+ *                     (g, u) = (gu[t][2i], gu[t][2i+1]) when interleaved,
+ *                     else (gu[t][i], gu[t][F+i])
+ * Strides are in elements; x, w, gu f32. */
+int b2a_rmsnorm_rows(const float* x, long long x_row_stride, const float* w, float eps, void* out,
+                     long long out_row_stride, int out_dtype, int n_rows, int E, void* stream);
+int b2a_swiglu_rows(const float* gu, long long gu_row_stride, int interleaved, void* out,
+                    long long out_row_stride, int out_dtype, int n_rows, int F, void* stream);
 
 #ifdef __cplusplus
 }

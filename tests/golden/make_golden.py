@@ -204,9 +204,19 @@ def make_llama_q8(model_mod):
     m.out_norm = c["out_norm"]
     m.output = qm(c["output"], V, E)
     m._init_cache()
+    import copy
+    fresh = copy.deepcopy(m)  # the same weights, untouched cache, for the batch path
     logits = np.stack([np.asarray(m._forward_np(t), dtype=np.float32) for t in c["tokens"]])
+    # the reference's batch path (Model.forward_batch, model.py:1274-1372) on
+    # the first five tokens as one chunk, then one decode token on top of it
+    n_chunk = 5
+    chunk_logits = np.asarray(fresh.forward_batch(c["tokens"][:n_chunk]), dtype=np.float32)
+    chunk_k0 = np.array(fresh.cache_k[0][:n_chunk], dtype=np.float32)
+    after_logits = np.asarray(fresh._forward_np(c["tokens"][n_chunk]), dtype=np.float32)
     np.savez_compressed(os.path.join(HERE, "llama_q8.npz"), weights_sha256=c["sha256"],
-                        tokens=np.array(c["tokens"], np.int32), logits=logits)
+                        tokens=np.array(c["tokens"], np.int32), logits=logits,
+                        n_chunk=n_chunk, chunk_logits=chunk_logits, chunk_k0=chunk_k0,
+                        after_chunk_logits=after_logits)
 
 
 def main():

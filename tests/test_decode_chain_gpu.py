@@ -25,7 +25,8 @@ def _q8(rng, rows, cols):
     return L.quantize_q8_0(rng.normal(0.0, 0.02, (rows, cols)).astype(np.float32))
 
 
-@pytest.mark.parametrize("rows,cols", [(1, 32), (3, 96), (300, 2048), (257, 8192)])
+@pytest.mark.parametrize("rows,cols", [(1, 32), (3, 96), (300, 2048), (257, 8192), (37, 6144),
+                                       (64, 4096)])
 @pytest.mark.parametrize("mode", [0, 1, 2])
 def test_q8_gemv_modes(cuda_dev, rows, cols, mode):
     from alpacca_open_sourced_by_jt_b200.decode_chain import Q8Matrix
@@ -82,7 +83,7 @@ def test_q8_embed_row(cuda_dev):
     for t in (0, 17, 49):
         tok = torch.tensor([t], dtype=torch.int32, device=cuda_dev)
         _lib.check(_lib.load().b2a_q8_embed(w.codes.data_ptr(), w.scales.data_ptr(), rows, cols,
-                                            tok.data_ptr(), out.data_ptr(), None))
+                                            tok.data_ptr(), 1, out.data_ptr(), None))
         torch.cuda.synchronize()
         assert np.array_equal(out.cpu().numpy(), L.q8_0_row(data, rows, cols, t))
 
