@@ -35,7 +35,9 @@ Also reported on the same line:
 
 Multi-GPU (torchrun, one rank per GPU): every rank decodes its own batch of
 16 sequences (sequence sharding, no collective on the data path), so
-scaling is weak; timing is the max over ranks of CUDA-event time.
+scaling is weak; timing is the max over ranks of CUDA-event time.  The
+single-GPU legs (kvstate, qwen35_layer, decode_step, prefill_chunk) run
+only when the job has one GPU.
 
 `--impl reference` times the reference's CPU implementation (the NumPy
 restatement in oracle/, the reference itself being Python that does not
@@ -683,16 +685,16 @@ def run_ours(args):
     if args.only in (None, "varlen"):
         vl = bench_varlen(dev, rank, world, args.steps, args.warmup, dist)
     kvs = None
-    if rank == 0 and args.only in (None, "kvstate"):
+    if world == 1 and args.only in (None, "kvstate"):
         kvs = bench_kvstate(dev, args.steps, args.warmup)
     q35 = None
-    if rank == 0 and args.only in (None, "qwen35"):
+    if world == 1 and args.only in (None, "qwen35"):
         q35 = bench_qwen35(dev, args.steps, args.warmup)
     c5 = None
-    if rank == 0 and args.only in (None, "decode_step"):
+    if world == 1 and args.only in (None, "decode_step"):
         c5 = bench_decode_step(dev, args.steps, args.warmup)
     pch = None
-    if rank == 0 and args.only in (None, "prefill_chunk"):
+    if world == 1 and args.only in (None, "prefill_chunk"):
         pch = bench_prefill_chunk(dev, args.steps, args.warmup)
     ms = st["ms"]
     if dist is not None:
