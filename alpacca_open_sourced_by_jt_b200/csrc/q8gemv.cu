@@ -4,30 +4,34 @@
 // The reference's Q8_0 matvec (alpaccaroo/qmatrix.py:312-320; its device
 // chain's kernel is cuda.py:241-286) computes, per output row r,
 //   out[r] = sum_b d[r][b] * sum_{l<32} q[r][32b+l] * x[32b+l]
-// with int8 codes q and f16 block scales d.  Here the GGUF records (an f16 d
-// then 32 codes, 34 bytes) are repacked once at load into an int8 code
-// matrix [rows][cols] (16-byte aligned rows) and an f16 scale matrix
-// [rows][cols/32]: the same 1.0625 bytes per weight, readable with 16-byte
-// loads.
+// with int8 codes q and f16 block scales d.
 //
-// HBM-bound: one lane owns one 32-code block per step (two 16-byte code
-// loads and one 2-byte scale load), each warp works two rows at once, and the
-// grid is persistent (the resident CTAs) over row pairs.  int8 -> f32 is one byte permute into
-// the mantissa of 2^23 and one subtraction (the conversion instruction runs
-// on the narrow XU pipe).  x is staged once per CTA in shared memory as
-// float4 column j of block b at [j][b], so a warp's 32 lanes read 32
-// consecutive float4s.  The staging applies the step's prologue:
+// The products run on the tensor cores (mma.sync m16n8k16, f16 in, f32
+// accumulate), which cuts the instructions per weight about fivefold against
+// an FMA loop: the A operand is 16 rows x 16 codes, each code turned exactly
+// into an f16 by one byte permute into 1024 + (code + 128) and one packed
+// subtraction; the B operand holds x split into f16 hi and lo parts
+// (x = hi + lo to about 2^-22) as its two used columns.  Per 32-code block
+// two MMAs give the block's dot for 16 rows; its f16 scale is applied in f32
+// and the rows accumulate in f32, as the reference sums blocks.
+//
+// Layout (repacked once at load from the GGUF records): rows are padded to a
+// multiple of 16 and cut into 512-byte tiles of 16 rows x one 32-code block,
+// tile (rg, b) at byte (rg * nb + b) * 512, lane t's 16 bytes being its A
+// fragments for the block's two MMAs (rows g = t/4 and g + 8, codes
+// 2(t%4) + {0, 1, 8, 9} and + 16); scales tile (rg, b) holds 16 f16 in the
+// order (row 0, row 8, row 1, row 9, ...).  A warp streams its tiles with
+// 16-byte loads, sixteen tiles in flight; rows longer than a few hundred
+// blocks are split across the warps of a CTA and meet in shared memory.
+// x is staged once per CTA, applying the step's prologue:
 //   RMSNORM  x * (1 / sqrt(x.x / n + eps)) * w   (tensor.py:349-356)
 //   SWIGLU   gate / (1 + exp(-gate)) * up          (model.py:1466-1467)
-// and the epilogue can add the product into out (the residual stream), or,
-// for a matrix whose rows interleave gate and up rows (2i = gate_i,
-// 2i+1 = up_i), write the SwiGLU of each row pair (the FFN's activation).
+// and the epilogue stores, adds into out (the residual stream) or, for a
+// matrix whose 16-row groups hold gate rows 8q..8q+7 then the matching up
+// rows, writes the SwiGLU of each (gate, up) row pair.
 //
-// Each warp walks its rows as slabs (a row pair x 64 blocks) with the next
-// slab's loads in flight while it computes the current one; rows longer
-// than 2048 columns are split across the warps of a CTA.  Chained
-// launches (flag B2A_GEMV_PDL) use programmatic dependent launch: every CTA
-// lets the next kernel launch at once and issues its first slab's loads
+// Chained launches (flag B2A_GEMV_PDL) use programmatic dependent launch:
+// every CTA lets the next kernel launch at once and loads its first tiles
 // (the weights do not depend on the previous kernel) before it waits for
 // the previous kernel and reads x.  Launched without the flag the wait
 // returns at once.
@@ -37,104 +41,64 @@ namespace q8 {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kRows = 2;  // rows per warp at a time
+constexpr int kUnroll = 16;  // tiles in flight per warp (a whole task when kw splits rows)
 
-__device__ __forceinline__ float code_f32(uint32_t biased_word, int k) {
-  // byte k of the word (code + 128) placed in the low mantissa bits of 2^23
-  return __uint_as_float(__byte_perm(biased_word, 0x4B000000u, 0x7440u + k)) - 8388736.0f;
+// two codes (bytes sel_lo/sel_hi of a word already biased by +128) -> f16x2
+__device__ __forceinline__ uint32_t codes_f16x2(uint32_t biased, uint32_t sel) {
+  const uint32_t v = __byte_perm(biased, 0x64646464u, sel);  // 1024 + (code + 128)
+  const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&v), __float2half2_rn(1152.f));
+  return *reinterpret_cast<const uint32_t*>(&r);
 }
 
-// sum_{l<32} code[l] * x[l] for one block: codes c0|c1 (2 x 16 bytes), x from
-// the staged [j][b] layout
-__device__ __forceinline__ float block_dot(const uint4& c0, const uint4& c1,
-                                           const float4* __restrict__ xs, int nb, int b) {
-  const uint32_t w[8] = {c0.x ^ 0x80808080u, c0.y ^ 0x80808080u, c0.z ^ 0x80808080u,
-                         c0.w ^ 0x80808080u, c1.x ^ 0x80808080u, c1.y ^ 0x80808080u,
-                         c1.z ^ 0x80808080u, c1.w ^ 0x80808080u};
-  float acc = 0.f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float4 xv = xs[j * nb + b];
-    acc = fmaf(code_f32(w[j], 0), xv.x, acc);
-    acc = fmaf(code_f32(w[j], 1), xv.y, acc);
-    acc = fmaf(code_f32(w[j], 2), xv.z, acc);
-    acc = fmaf(code_f32(w[j], 3), xv.w, acc);
-  }
-  return acc;
-}
-
-// Epilogues: 0 store, 1 add into out (residual), 2 SwiGLU of the row pair
 template <int Mode, int Epi>
 __global__ void __launch_bounds__(kThreads) gemv_kernel(
-    const int8_t* __restrict__ codes, const __half* __restrict__ scales, int rows, int cols,
-    const float* __restrict__ x, const float* __restrict__ aux, float eps,
+    const uint4* __restrict__ tiles, const uint32_t* __restrict__ scales, int rows, int cols,
+    int kw, const float* __restrict__ x, const float* __restrict__ aux, float eps,
     float* __restrict__ out) {
-  extern __shared__ float4 xs[];  // [8][nb]
+  extern __shared__ uint4 xs[];  // [nb][8]: B fragments (hi for lanes 0-3, lo for 4-7)
   __shared__ double red[kWarps];
+  __shared__ float psum[2][kWarps][16];
   const int nb = cols >> 5;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, tp = lane & 3;
+  const int rgs = (rows + 15) >> 4;   // row groups
+  const int slots = kWarps / kw;      // row groups per CTA task
+  const int slot = warp / kw, ks = warp % kw;
+  const int bpw = (nb + kw - 1) / kw;  // blocks per warp
+  const int b_lo = ks * bpw, b_hi = min(nb, b_lo + bpw);
+  const int tasks = (rgs + slots - 1) / slots;
+  const int n_tasks = static_cast<int>(blockIdx.x) < tasks
+                          ? (tasks - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1
+                          : 0;
 
-  // Work unit: a slab = one row pair x 64 blocks (lane l: blocks
-  // part*64 + l and part*64 + 32 + l of both rows, 128 bytes of codes).  A
-  // row pair has spp = ceil(nb/64) slabs, taken by spp warps of the same CTA
-  // (a long row is split across warps, their sums meet in shared memory),
-  // so a CTA round covers ppr = kWarps / spp pairs.  Each warp walks its
-  // rounds with the next round's slab loads in flight while it computes the
-  // current one.
-  const int spp = (nb + 63) >> 6;
-  const int ppr = kWarps / spp;
-  const int wpair = warp / spp, wpart = warp % spp;
-  const bool wactive = wpair < ppr;
-  const int pairs = (rows + kRows - 1) / kRows;
-  const int groups = (pairs + ppr - 1) / ppr;
-  const int n_rounds = static_cast<int>(blockIdx.x) < groups
-                           ? (groups - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1
-                           : 0;
-  __shared__ float psum[2][kWarps][kRows];  // per round parity
-
-  struct Slab {
-    uint4 c[kRows][2][2];
-    float d[kRows][2];
-  };
-  // pair handled by this warp in round j (>= pairs: none)
-  auto pair_of = [&](int j) { return (blockIdx.x + j * gridDim.x) * ppr + wpair; };
-  auto load = [&](int j, Slab& sl) {
-    const int pr = pair_of(j);
-    const bool live = wactive && pr < pairs;
-    const int r0 = pr * kRows;
+  uint4 c[kUnroll];
+  uint32_t sc[kUnroll];
+  auto load = [&](int rg, int b0) {
 #pragma unroll
-    for (int r = 0; r < kRows; ++r) {
-      const int row = min(r0 + r, rows - 1);
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int blk = wpart * 64 + h * 32 + lane;
-        if (live && blk < nb) {
-          const uint4* p = reinterpret_cast<const uint4*>(codes + static_cast<size_t>(row) * cols +
-                                                          blk * 32);
-          sl.c[r][h][0] = __ldg(p);
-          sl.c[r][h][1] = __ldg(p + 1);
-          sl.d[r][h] = __half2float(scales[static_cast<size_t>(row) * nb + blk]);
-        } else {
-          sl.c[r][h][0] = sl.c[r][h][1] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u,
-                                                     0x80808080u);  // codes 0 after the bias
-          sl.d[r][h] = 0.f;
-        }
+    for (int u = 0; u < kUnroll; ++u) {
+      const int b = b0 + u;
+      if (rg < rgs && b < b_hi) {
+        const size_t t = static_cast<size_t>(rg) * nb + b;
+        c[u] = __ldg(tiles + t * 32 + lane);
+        sc[u] = tp == 0 ? __ldg(scales + t * 8 + g) : 0u;
+      } else {
+        c[u] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);  // codes 0
+        sc[u] = 0u;
       }
     }
   };
 
   // ---- overlap with the previous kernel: release the next, load weights ---
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  Slab cur, nxt;
-  if (n_rounds > 0) load(0, cur);  // weights do not depend on the previous kernel
+  if (n_tasks > 0) load(static_cast<int>(blockIdx.x) * slots + slot, b_lo);
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  // ---- stage x (with the prologue) ---------------------------------------
+  // ---- stage x (with the prologue) as f16 hi / lo B fragments -----------------
   float scale = 1.f;
   if (Mode == 1) {
     double ss = 0.0;
-    for (int c = threadIdx.x; c < cols; c += kThreads) {
-      const double v = x[c];
+    for (int i = threadIdx.x; i < cols; i += kThreads) {
+      const double v = x[i];
       ss += v * v;
     }
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -145,76 +109,84 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(
     for (int i = 0; i < kWarps; ++i) tot += red[i];
     scale = static_cast<float>(1.0 / sqrt(tot / cols + static_cast<double>(eps)));
   }
-  for (int i = threadIdx.x; i < nb * 8; i += kThreads) {
-    const int b = i >> 3, j = i & 7;  // float4 j of block b
-    const int c = b * 32 + j * 4;
-    float4 v;
+  auto xin = [&](int i) -> float {
     if (Mode == 2) {
-      float e[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float g = x[c + t];
-        e[t] = g / (1.f + expf(-g)) * x[cols + c + t];
-      }
-      v = make_float4(e[0], e[1], e[2], e[3]);
-    } else {
-      v = *reinterpret_cast<const float4*>(x + c);
-      if (Mode == 1) {
-        const float4 w = *reinterpret_cast<const float4*>(aux + c);
-        v = make_float4(v.x * scale * w.x, v.y * scale * w.y, v.z * scale * w.z,
-                        v.w * scale * w.w);
-      }
+      const float gt = x[i];
+      return gt / (1.f + expf(-gt)) * x[cols + i];
     }
-    xs[j * nb + b] = v;
+    const float v = x[i];
+    return Mode == 1 ? v * scale * aux[i] : v;
+  };
+  for (int i = threadIdx.x; i < nb * 8; i += kThreads) {
+    const int b = i >> 3, e = i & 7, lo = e >> 2, q = e & 3;
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {  // MMA0 b0, MMA0 b1, MMA1 b0, MMA1 b1
+      const int k = 32 * b + (j >> 1) * 16 + (j & 1) * 8 + 2 * q;
+      const float v0 = xin(k), v1 = xin(k + 1);
+      const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+      const __half2 hv = lo ? __floats2half2_rn(v0 - __half2float(h0), v1 - __half2float(h1))
+                            : __halves2half2(h0, h1);
+      w[j] = *reinterpret_cast<const uint32_t*>(&hv);
+    }
+    xs[i] = make_uint4(w[0], w[1], w[2], w[3]);
   }
   __syncthreads();
 
-  // ---- rounds --------------------------------------------------------------
-  for (int j = 0; j < n_rounds; ++j) {
-    if (j + 1 < n_rounds) load(j + 1, nxt);
-    float acc[kRows] = {0.f, 0.f};
+  // ---- tasks ---------------------------------------------------------------
+  for (int j = 0; j < n_tasks; ++j) {
+    const int rg = (static_cast<int>(blockIdx.x) + j * gridDim.x) * slots + slot;
+    float acc_a = 0.f, acc_b = 0.f;  // rows 16rg + g and 16rg + g + 8 (lanes tp == 0)
+    for (int b0 = b_lo; b0 < b_hi; b0 += kUnroll) {
+      if (b0 != b_lo) load(rg, b0);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int blk = wpart * 64 + h * 32 + lane;
-      if (blk < nb) {
-#pragma unroll
-        for (int r = 0; r < kRows; ++r)
-          acc[r] = fmaf(block_dot(cur.c[r][h][0], cur.c[r][h][1], xs, nb, blk), cur.d[r][h],
-                        acc[r]);
+      for (int u = 0; u < kUnroll; ++u) {
+        const int b = b0 + u;
+        if (b >= b_hi) break;
+        const uint4 bf = lane < 8 ? xs[b * 8 + lane] : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t w0 = c[u].x ^ 0x80808080u, w1 = c[u].y ^ 0x80808080u;
+        const uint32_t w2 = c[u].z ^ 0x80808080u, w3 = c[u].w ^ 0x80808080u;
+        const uint32_t a0[4] = {codes_f16x2(w0, 0x4140u), codes_f16x2(w0, 0x4342u),
+                                codes_f16x2(w1, 0x4140u), codes_f16x2(w1, 0x4342u)};
+        const uint32_t a1[4] = {codes_f16x2(w2, 0x4140u), codes_f16x2(w2, 0x4342u),
+                                codes_f16x2(w3, 0x4140u), codes_f16x2(w3, 0x4342u)};
+        const uint32_t b0f[2] = {bf.x, bf.y}, b1f[2] = {bf.z, bf.w};
+        float cc[4] = {0.f, 0.f, 0.f, 0.f};
+        MmaOp<__half>::run(cc, a0, b0f);
+        MmaOp<__half>::run(cc, a1, b1f);
+        const __half2 d = *reinterpret_cast<const __half2*>(&sc[u]);  // rows g, g + 8
+        acc_a = fmaf(cc[0] + cc[1], __low2float(d), acc_a);
+        acc_b = fmaf(cc[2] + cc[3], __high2float(d), acc_b);
       }
     }
-#pragma unroll
-    for (int r = 0; r < kRows; ++r)
-      for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
-    if (spp > 1) {
-      if (lane == 0) {
-        psum[j & 1][warp][0] = acc[0];
-        psum[j & 1][warp][1] = acc[1];
+    if (j + 1 < n_tasks)  // next task's first tiles while the epilogue runs
+      load((static_cast<int>(blockIdx.x) + (j + 1) * gridDim.x) * slots + slot, b_lo);
+    if (kw > 1) {
+      if (tp == 0) {
+        psum[j & 1][warp][g] = acc_a;
+        psum[j & 1][warp][g + 8] = acc_b;
       }
       __syncthreads();
-      if (wactive && wpart == 0) {  // the pair's first warp adds its siblings' sums in order
-        for (int t = 1; t < spp; ++t) {
-          acc[0] += psum[j & 1][warp + t][0];
-          acc[1] += psum[j & 1][warp + t][1];
+      if (ks == 0 && tp == 0) {  // the group's first warp adds its siblings' sums in order
+        for (int t = 1; t < kw; ++t) {
+          acc_a += psum[j & 1][warp + t][g];
+          acc_b += psum[j & 1][warp + t][g + 8];
         }
       }
     }
-    const int pr = pair_of(j);
-    if (wactive && wpart == 0 && lane == 0 && pr < pairs) {
-      const int r0 = pr * kRows;
-      const bool two = r0 + 1 < rows;
-      const float a0 = acc[0], a1 = acc[1];
-      if (Epi == 1) {
-        out[r0] += a0;
-        if (two) out[r0 + 1] += a1;
-      } else if (Epi == 2) {
-        out[r0 >> 1] = a0 / (1.f + expf(-a0)) * a1;  // gate_i = row 2i, up_i = row 2i+1
+    if (ks == 0 && tp == 0 && rg < rgs) {
+      const int ra = rg * 16 + g, rb = ra + 8;
+      if (Epi == 2) {
+        const int i = rg * 8 + g;  // gate row ra, up row rb
+        if (rb < rows) out[i] = acc_a / (1.f + expf(-acc_a)) * acc_b;
+      } else if (Epi == 1) {
+        if (ra < rows) out[ra] += acc_a;
+        if (rb < rows) out[rb] += acc_b;
       } else {
-        out[r0] = a0;
-        if (two) out[r0 + 1] = a1;
+        if (ra < rows) out[ra] = acc_a;
+        if (rb < rows) out[rb] = acc_b;
       }
     }
-    if (j + 1 < n_rounds) cur = nxt;
   }
 }
 
@@ -245,7 +217,7 @@ int launch_gemv(const int8_t* codes, const __half* scales, int rows, int cols, c
                 const float* aux, float eps, float* out, bool pdl, cudaStream_t st) {
   namespace Q = b2a::q8;
   auto kern = Q::gemv_kernel<Mode, Epi>;
-  const int smem = cols * 4;  // 8 float4 per 32-column block
+  const int smem = cols * 4;  // 8 uint4 B fragments per 32-column block
   if (smem > 48 * 1024) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                smem);
@@ -254,10 +226,14 @@ int launch_gemv(const int8_t* codes, const __half* scales, int rows, int cols, c
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int pairs = (rows + Q::kRows - 1) / Q::kRows;
-  const int ppr = Q::kWarps / ((cols / 32 + 63) / 64);  // pairs per CTA round
-  int grid = (pairs + ppr - 1) / ppr;
-  int per_sm = 1;  // persistent: at most the resident CTAs, each walks its pairs
+  // split each row group's blocks over kw warps until there are ~4096 warp
+  // tasks (kw a power of two dividing the CTA's 8 warps, >= 8 blocks each)
+  const int rgs = (rows + 15) / 16, nb = cols / 32;
+  int kw = 1;
+  while (kw < Q::kWarps && rgs * kw < 4096 && nb / (2 * kw) >= 8) kw *= 2;
+  const int slots = Q::kWarps / kw;
+  int grid = (rgs + slots - 1) / slots;
+  int per_sm = 1;  // persistent: at most the resident CTAs, each walks its tasks
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Q::kThreads, smem);
   if (per_sm < 1) per_sm = 1;
   if (grid > sms * per_sm) grid = sms * per_sm;
@@ -271,7 +247,9 @@ int launch_gemv(const int8_t* codes, const __half* scales, int rows, int cols, c
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, codes, scales, rows, cols, x, aux, eps, out);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, reinterpret_cast<const uint4*>(codes),
+                                           reinterpret_cast<const uint32_t*>(scales), rows, cols,
+                                           kw, x, aux, eps, out);
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "q8_gemv launch");
   return B2A_OK;
 }
@@ -288,9 +266,9 @@ int b2a_q8_gemv(const void* codes, const void* scales, int rows, int cols, const
     return fail(B2A_ERR_SHAPE, "q8_gemv: rows %d, cols %d (cols a positive multiple of 32)", rows,
                 cols);
   if (cols > 16384) return fail(B2A_ERR_UNSUPPORTED, "q8_gemv: cols %d > 16384", cols);
-  if (!b2a_host::aligned16(codes) || (reinterpret_cast<uintptr_t>(scales) & 1) ||
+  if (!b2a_host::aligned16(codes) || (reinterpret_cast<uintptr_t>(scales) & 3) ||
       !b2a_host::aligned16(x))
-    return fail(B2A_ERR_ALIGN, "q8_gemv: codes and x must be 16-byte aligned, scales 2-byte");
+    return fail(B2A_ERR_ALIGN, "q8_gemv: tiles and x must be 16-byte aligned, scales 4-byte");
   if (mode < 0 || mode > 2) return fail(B2A_ERR_ARG, "q8_gemv: mode %d", mode);
   if (mode == 1 && (!aux || !b2a_host::aligned16(aux) || !(eps > 0.f)))
     return fail(B2A_ERR_ARG, "q8_gemv: RMSNorm needs an aligned weight and eps > 0");
@@ -300,7 +278,8 @@ int b2a_q8_gemv(const void* codes, const void* scales, int rows, int cols, const
     return fail(B2A_ERR_ARG, "q8_gemv: unknown flags %#x", flags);
   const bool acc = flags & B2A_GEMV_ACCUMULATE, swo = flags & B2A_GEMV_SWIGLU_OUT;
   if (acc && swo) return fail(B2A_ERR_ARG, "q8_gemv: ACCUMULATE and SWIGLU_OUT exclude each other");
-  if (swo && (rows & 1)) return fail(B2A_ERR_SHAPE, "q8_gemv: SWIGLU_OUT needs an even row count");
+  if (swo && (rows & 15))
+    return fail(B2A_ERR_SHAPE, "q8_gemv: SWIGLU_OUT needs whole 16-row (8 gate + 8 up) groups");
   const bool pdl = flags & B2A_GEMV_PDL;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int epi = acc ? 1 : (swo ? 2 : 0);

@@ -35,9 +35,31 @@ _Q8_0 = np.dtype([("d", "<f2"), ("qs", "i1", 32)])
 ACCUMULATE, SWIGLU_OUT, PDL = 1, 2, 4  # b2a_q8_gemv flags
 
 
+def _fragment_order():
+    """Byte order of a 16-row x 32-code tile as b2a_q8_gemv reads it: lane t
+    (g = t/4, q = t%4) holds the A fragments of the block's two m16n8k16
+    MMAs, registers a0..a3 = (row g | g+8) x (codes 2q, 2q+1 | 2q+8, 2q+9),
+    codes + 16 for the second MMA."""
+    rows, ks = [], []
+    for t in range(32):
+        g, q = t // 4, t % 4
+        for j in range(16):
+            m, reg, half = j // 8, (j % 8) // 2, j % 2
+            rows.append(g + (8 if reg in (1, 3) else 0))
+            ks.append(16 * m + 2 * q + half + (8 if reg in (2, 3) else 0))
+    return rows, ks
+
+
+_FRAG_ROWS, _FRAG_KS = _fragment_order()
+_SCALE_ORDER = [r for g in range(8) for r in (g, g + 8)]
+
+
 class Q8Matrix:
-    """A Q8_0 matrix repacked for the device: codes int8 (rows, cols) and
-    scales f16 (rows, cols/32)."""
+    """A Q8_0 matrix on the device: codes int8 (rows, cols) and scales f16
+    (rows, cols/32) row-major (the embedding gather and dequantized copies
+    read these), and, built on first use, the tiles b2a_q8_gemv streams:
+    rows padded to 16, 512-byte tiles of 16 rows x one 32-code block in MMA
+    fragment order, scales 16 per tile ordered (row 0, 8, 1, 9, ...)."""
 
     def __init__(self, codes: torch.Tensor, scales: torch.Tensor):
         if codes.dtype != torch.int8 or scales.dtype != torch.float16 or codes.dim() != 2:
@@ -46,6 +68,26 @@ class Q8Matrix:
         if self.cols % 32 or tuple(scales.shape) != (self.rows, self.cols // 32):
             raise _lib.B2AShapeError(_lib.ERR_SHAPE, "scales must be (rows, cols / 32)")
         self.codes, self.scales = codes.contiguous(), scales.contiguous()
+        self._tiles = None
+
+    def tiles(self):
+        """(tiles int8 (groups, nb, 512), tile scales f16 (groups, nb, 16))."""
+        if self._tiles is None:
+            R, C = self.rows, self.cols
+            nb, rg = C // 32, (R + 15) // 16
+            codes, scales = self.codes, self.scales
+            if rg * 16 != R:
+                pad = rg * 16 - R
+                codes = torch.cat([codes, codes.new_zeros((pad, C))])
+                scales = torch.cat([scales, scales.new_zeros((pad, nb))])
+            dev = codes.device
+            t = codes.view(rg, 16, nb, 32).permute(0, 2, 1, 3)
+            tiles = t[:, :, torch.tensor(_FRAG_ROWS, device=dev),
+                      torch.tensor(_FRAG_KS, device=dev)].contiguous()
+            ts = scales.view(rg, 16, nb).permute(0, 2, 1)[:, :, torch.tensor(_SCALE_ORDER,
+                                                                             device=dev)]
+            self._tiles = (tiles, ts.contiguous())
+        return self._tiles
 
     @classmethod
     def from_q8_0(cls, data: bytes, rows: int, cols: int, dev) -> "Q8Matrix":
@@ -77,20 +119,28 @@ class Q8Matrix:
 
     @staticmethod
     def interleave(a: "Q8Matrix", b: "Q8Matrix") -> "Q8Matrix":
-        """Rows a0, b0, a1, b1, ... (the FFN's gate and up rows side by side,
-        so one warp's row pair yields one SwiGLU output)."""
-        return Q8Matrix(torch.stack((a.codes, b.codes), 1).reshape(-1, a.cols),
-                        torch.stack((a.scales, b.scales), 1).reshape(-1, a.cols // 32))
+        """Rows a0..a7, b0..b7, a8..a15, b8..b15, ... (the FFN's gate and up
+        rows in one 16-row group, so the GEMV's SWIGLU_OUT epilogue finds
+        gate i and up i in the same lane).  Row counts a multiple of 8."""
+        if a.rows % 8 or a.rows != b.rows or a.cols != b.cols:
+            raise _lib.B2AShapeError(_lib.ERR_SHAPE, "interleave: equal shapes, rows % 8 == 0")
+        n, c, nb = a.rows // 8, a.cols, a.cols // 32
+        return Q8Matrix(torch.stack((a.codes.view(n, 8, c), b.codes.view(n, 8, c)), 1)
+                        .reshape(-1, c),
+                        torch.stack((a.scales.view(n, 8, nb), b.scales.view(n, 8, nb)), 1)
+                        .reshape(-1, nb))
 
     def nbytes(self) -> int:
+        """Bytes a GEMV streams: the codes and scales of every row."""
         return self.codes.numel() + self.scales.numel() * 2
 
     def gemv(self, x: torch.Tensor, out: torch.Tensor, *, mode: int = 0, aux=None,
              eps: float = 0.0, flags: int = 0, stream=None) -> torch.Tensor:
         """out = self . xin (mode 0: x, 1: RMSNorm(x, aux, eps), 2: SwiGLU of
         x's two halves); flags ACCUMULATE / SWIGLU_OUT / PDL (b2a_q8_gemv)."""
+        tiles, ts = self.tiles()
         _lib.check(_lib.load().b2a_q8_gemv(
-            self.codes.data_ptr(), self.scales.data_ptr(), self.rows, self.cols, x.data_ptr(),
+            tiles.data_ptr(), ts.data_ptr(), self.rows, self.cols, x.data_ptr(),
             None if aux is None else aux.data_ptr(), mode, float(eps), out.data_ptr(),
             int(flags), device._stream(stream)))
         return out

@@ -18,7 +18,7 @@ straight into a DecodeChain's caches, so decoding continues from it:
     att  = causal prefill over cache rows 0..pos0+T-1  b2a_prefill (tcgen05)
     x   += att . Wo^T      tensor-core GEMM with the residual as its C input
     h    = RMSNorm(x)      b2a_rmsnorm_rows
-    gu   = h . Wgu^T       (gate/up rows interleaved)
+    gu   = h . Wgu^T       ([gate rows; up rows])
     act  = SwiGLU(gu)      b2a_swiglu_rows
     x   += act . Wdown^T
   logits = Woutput . RMSNorm(x[T-1])   b2a_q8_gemv (the decode path's Q8_0 GEMV)
@@ -59,7 +59,8 @@ class ChunkPrefill:
         dev = m.device
         self.max_chunk = int(max_chunk)
         self.w = [dict(qkv=_dequant(ly["wqkv"], dt), wo=_dequant(ly["wo"], dt),
-                       gu=_dequant(ly["wgu"], dt), down=_dequant(ly["w_down"], dt))
+                       gu=self._gate_up(_dequant(ly["wgu"], dt), m.F),
+                       down=_dequant(ly["w_down"], dt))
                   for ly in m.layers]
         T, E, H, KV, D, F = self.max_chunk, m.E, m.H, m.KV, m.D, m.F
         self.x = torch.zeros((T, E), dtype=torch.float32, device=dev)
@@ -70,6 +71,13 @@ class ChunkPrefill:
         self.tokens = torch.zeros(T, dtype=torch.int32, device=dev)
         self.positions = torch.zeros(T, dtype=torch.int32, device=dev)
         self.logits = torch.zeros(m.V, dtype=torch.float32, device=dev)
+
+    @staticmethod
+    def _gate_up(w: torch.Tensor, F: int) -> torch.Tensor:
+        """The decode path's gate/up matrix (8 gate rows, 8 up rows, ...) as
+        [all gate rows; all up rows] for the chunk GEMM."""
+        g = w.view(F // 8, 2, 8, -1)
+        return torch.cat([g[:, 0].reshape(F, -1), g[:, 1].reshape(F, -1)]).contiguous()
 
     def _norm(self, x, w, T):
         m = self.m
@@ -114,7 +122,7 @@ class ChunkPrefill:
             x.copy_(torch.addmm(x, att.view(T, qd), w["wo"].t(), out_dtype=torch.float32))
             h = self._norm(x, ly["ffn_norm"], T)
             gu = torch.mm(h, w["gu"].t(), out_dtype=torch.float32)
-            _lib.check(lib.b2a_swiglu_rows(gu.data_ptr(), 2 * m.F, 1, self.act.data_ptr(), m.F,
+            _lib.check(lib.b2a_swiglu_rows(gu.data_ptr(), 2 * m.F, 0, self.act.data_ptr(), m.F,
                                            self.code, T, m.F, st))
             x.copy_(torch.addmm(x, self.act[:T], w["down"].t(), out_dtype=torch.float32))
         if not want_logits:

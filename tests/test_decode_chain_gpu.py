@@ -26,7 +26,7 @@ def _q8(rng, rows, cols):
 
 
 @pytest.mark.parametrize("rows,cols", [(1, 32), (3, 96), (300, 2048), (257, 8192), (37, 6144),
-                                       (64, 4096)])
+                                       (64, 4096), (17, 512), (2000, 256)])
 @pytest.mark.parametrize("mode", [0, 1, 2])
 def test_q8_gemv_modes(cuda_dev, rows, cols, mode):
     from alpacca_open_sourced_by_jt_b200.decode_chain import Q8Matrix
@@ -55,7 +55,7 @@ def test_q8_gemv_modes(cuda_dev, rows, cols, mode):
     assert rel_err(out.cpu().numpy(), base + want) < 1e-5
 
 
-@pytest.mark.parametrize("rows,cols", [(2, 64), (512, 2048)])
+@pytest.mark.parametrize("rows,cols", [(8, 64), (512, 2048), (40, 8192)])
 def test_q8_gemv_swiglu_epilogue(cuda_dev, rows, cols):
     from alpacca_open_sourced_by_jt_b200.decode_chain import Q8Matrix
     rng = np.random.default_rng(rows + cols)
