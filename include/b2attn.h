@@ -250,7 +250,7 @@ int b2a_sigmoid_gate(const float* values, long long value_row_stride, const floa
 
 /* b2a_q8_gemv flags */
 #define B2A_GEMV_ACCUMULATE 1 /* out[r] += product (the residual stream) */
-#define B2A_GEMV_SWIGLU_OUT 2 /* rows interleave gate/up: out[i] = silu(row 2i) * row 2i+1 */
+#define B2A_GEMV_SWIGLU_OUT 2 /* 16-row groups of 8 gate + 8 up rows: out = silu(gate) * up */
 #define B2A_GEMV_PDL 4        /* launch as a programmatic dependent of the previous kernel */
 
 /* Q8_0 matrix-vector product for a decode step (batch 1):
@@ -262,15 +262,20 @@ int b2a_sigmoid_gate(const float* values, long long value_row_stride, const floa
  *           tensor.py:349-356; aux = the norm weight)
  *   mode 2  xin = g / (1 + exp(-g)) * u, g = x[0:cols], u = x[cols:2cols]
  *           (SwiGLU, model.py:1466-1467)
- flags: B2A_GEMV_ACCUMULATE adds into out (the residual stream);
+ * flags: B2A_GEMV_ACCUMULATE adds into out (the residual stream);
  * B2A_GEMV_SWIGLU_OUT, for a matrix whose rows interleave the FFN's gate and
- * up rows, writes out[i] = g/(1+exp(-g))*u of the row pair (rows/2 values);
+ * up rows, writes g/(1+exp(-g))*u of each (gate, up) row pair (rows/2 values);
  * B2A_GEMV_PDL launches the kernel as a programmatic dependent of the
- * previous kernel on the stream: it prefetches its weights into L2 while
+ * previous kernel on the stream: it loads its first weight tiles while
  * that kernel finishes and reads x only after it completed.  Weights are the
- * Q8_0 records repacked: codes int8 [rows][cols] (16-byte aligned rows),
- * scales f16 [rows][cols/32].  cols a multiple of 32, <= 16384; codes, x
- * and aux 16-byte aligned. */
+ * Q8_0 records repacked once: rows padded to a multiple of 16 and cut into
+ * 512-byte tiles of 16 rows x one 32-code block, tile (rg, b) at byte
+ * (rg * cols/32 + b) * 512 in mma.sync m16n8k16 A-fragment order (lane t's
+ * 16 bytes: rows t/4 and t/4 + 8, codes 2(t%4) + {0, 1, 8, 9}, then + 16);
+ * scales f16, 16 per tile in the order (row 0, row 8, row 1, row 9, ...).
+ * For B2A_GEMV_SWIGLU_OUT each 16-row group holds 8 gate rows then the
+ * matching 8 up rows (rows a multiple of 16).  cols a multiple of 32,
+ * <= 16384; tiles, x and aux 16-byte aligned, scales 4-byte aligned. */
 int b2a_q8_gemv(const void* codes, const void* scales, int rows, int cols, const float* x,
                 const float* aux, int mode, float eps, float* out, int flags, void* stream);
 
