@@ -19,6 +19,7 @@ ROPE_NORM, ROPE_NEOX = 0, 1
 OK = 0
 ERR_ARG, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_UNSUPPORTED = 1, 2, 3, 4, 5
 ERR_WORKSPACE, ERR_CUDA, ERR_TIMEOUT, ERR_POSITION = 6, 7, 8, 9
+LAUNCH_PDL = 1  # b2a_set_launch_flags
 
 _NAMES = {
     ERR_ARG: "invalid argument", ERR_SHAPE: "shape", ERR_DTYPE: "dtype",
@@ -48,6 +49,7 @@ SIGNATURES = [
     ("b2a_version", c_int, []),
     ("b2a_last_error", c_char_p, []),
     ("b2a_device_error", c_int, [POINTER(c_int), POINTER(c_int), c_int]),
+    ("b2a_set_launch_flags", c_int, [c_int]),
     ("b2a_decode_workspace_bytes", c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     ("b2a_decode_split_rows", c_int, [c_int, c_int, c_int, c_int]),
     ("b2a_decode", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

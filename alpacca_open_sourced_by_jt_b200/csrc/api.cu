@@ -7,6 +7,7 @@
 
 namespace {
 thread_local char t_last_error[512] = "";
+thread_local int t_launch_flags = 0;
 
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                     const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -75,11 +76,19 @@ int make_tmap(CUtensorMap* out, CUtensorMapDataType dtype, int rank, void* base,
   return B2A_OK;
 }
 
+int launch_flags() { return t_launch_flags; }
+
 }  // namespace b2a_host
 
 extern "C" {
 
 int b2a_version(void) { return B2A_ABI_VERSION; }
+
+int b2a_set_launch_flags(int flags) {
+  const int old = t_launch_flags;
+  t_launch_flags = flags & B2A_LAUNCH_PDL;
+  return old;
+}
 
 const char* b2a_last_error(void) { return t_last_error; }
 

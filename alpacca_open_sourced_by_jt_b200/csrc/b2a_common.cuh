@@ -11,6 +11,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/b2attn.h"
 
 namespace b2a {
@@ -195,6 +197,11 @@ __device__ __forceinline__ void st_elem(float* p, float v) { *p = v; }
 __device__ __forceinline__ void st_elem(__half* p, float v) { *p = __float2half_rn(v); }
 __device__ __forceinline__ void st_elem(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
 
+// Wait until the kernel this one was launched after (as a programmatic
+// dependent) has completed and its writes are visible; returns at once for
+// an ordinary launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // 2^x with the SFU instruction (PTX ex2.approx.ftz.f32: relative error about
 // 2^-22, ex2(-inf) = +0).  The softmax kernels feed it max-subtracted scores.
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -223,5 +230,27 @@ int make_tmap(CUtensorMap* out, CUtensorMapDataType dtype, int rank, void* base,
 
 int elem_size(int dtype);
 bool aligned16(const void* p);
+
+// The calling thread's b2a_set_launch_flags value.
+int launch_flags();
+
+// Launch `kern`, as a programmatic dependent of the stream's previous kernel
+// when the thread's launch flags ask for it (the kernel then waits with
+// griddepcontrol.wait before reading that kernel's output).
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                   Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (launch_flags() & B2A_LAUNCH_PDL) ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 }  // namespace b2a_host

@@ -64,9 +64,10 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
     const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
     const float* __restrict__ q, const int* __restrict__ lens, float* __restrict__ part_o,
     float* __restrict__ part_ml, int H, int group, int split_rows, int n_splits, float qscale) {
-  // a programmatic dependent launched after this kernel may start its
-  // independent prologue now (it waits for this kernel before reading)
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // The kernels after this one (a PDL chain) are released only once every
+  // CTA has streamed its rows (end of the main loop, below): released at
+  // entry, they would start their own weight prefetches and take HBM
+  // bandwidth from this kernel, which is the step's critical path.
   using C = Cfg<D>;
   constexpr int KS = D / 16;  // k-steps of QK^T, m-tiles of PV
   extern __shared__ uint8_t smem_raw[];
@@ -97,14 +98,22 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
     if (lane == 0) {
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
+      // Rows below len - 1 were appended by earlier steps: under a
+      // programmatic launch they stream before the wait for the kernel
+      // before (the step's RoPE + append, which writes row len - 1).
+      bool waited = false;
       for (int it = 0; it < n_tiles; ++it) {
         const int s = it % C::kStages;
         const uint32_t ph = (it / C::kStages) & 1;
         if (it >= C::kStages && !mbar_wait(&empty_bar[s], ph ^ 1, 0x100 | s)) break;
+        const int r = row0 + it * kRows;
+        if (!waited && r + kRows >= len) {
+          pdl_wait();
+          waited = true;
+        }
         mbar_arrive_expect_tx(&full_bar[s], C::kStageBytes);
         uint8_t* kt = smem + s * C::kStageBytes;
         uint8_t* vt = kt + C::kTileBytes;
-        const int r = row0 + it * kRows;
 #pragma unroll
         for (int bx = 0; bx < C::kBoxes; ++bx) {
           tma_load_4d(kt + bx * C::kBoxBytes, &tmK, &full_bar[s], bx * 64, kvh, r, b);
@@ -116,6 +125,7 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
   }
 
   // ---------------- consumer warps --------------------------------------
+  pdl_wait();  // q comes from the kernel before (a no-op unless PDL-launched)
   const int g = lane >> 2, t = lane & 3;
   // Query fragments (B operand of S^T = K.Q^T), pre-scaled by scale*log2(e)
   // so the softmax runs on exp2.  Heads >= group are zero padding.
@@ -258,6 +268,8 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
     if (lane == 0) mbar_arrive(&empty_bar[s]);
   }
 
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
   // ---------------- merge the four warps' partial softmax states ----------
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
@@ -332,6 +344,8 @@ __global__ void __launch_bounds__(kFmaWarps * 32) decode_fma_kernel(
     const float* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc,
     const int* __restrict__ lens, float* __restrict__ part_o, float* __restrict__ part_ml, int H,
     int KV, int group, long long seq_stride, int split_rows, int n_splits, float qscale) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  pdl_wait();  // q and the newest rows come from the kernels before
   constexpr int D = DL * 32;
   extern __shared__ float fsm[];
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -432,6 +446,7 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(
   // a programmatic dependent launched after this kernel may start its
   // independent prologue now (it waits for this kernel before reading)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  pdl_wait();  // the partials come from the split kernel before
   extern __shared__ float wsm[];  // [n_splits] weights
   __shared__ float red[kCombineThreads / 32];
   __shared__ float s_M, s_invL;
@@ -490,6 +505,8 @@ __global__ void lse_combine_kernel(const float* __restrict__ o_parts, long long 
                                    const float* __restrict__ lse_parts, long long lse_stride,
                                    int G, int rows, int D, float* __restrict__ out,
                                    float* __restrict__ lse_out) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  pdl_wait();  // the parts may come from the kernel before
   const int r = blockIdx.x;
   float M = -INFINITY;
   for (int g = 0; g < G; ++g) M = fmaxf(M, lse_parts[g * lse_stride + r]);
@@ -554,8 +571,9 @@ int launch_mma(const CUtensorMap& tk, const CUtensorMap& tv, const float* q, con
     if (dev < 64) configured |= (1ull << dev);
   }
   dim3 grid(n_splits, KV, B);
-  kern<<<grid, Dk::kThreads, smem, st>>>(tk, tv, q, lens, part_o, part_ml, H, group, split_rows,
-                                     n_splits, qscale);
+  const cudaError_t e = b2a_host::launch(kern, grid, dim3(Dk::kThreads), smem, st, tk, tv, q, lens,
+                                         part_o, part_ml, H, group, split_rows, n_splits, qscale);
+  if (e != cudaSuccess) return b2a_host::cuda_fail(e, "decode launch");
   return B2A_OK;
 }
 
@@ -599,8 +617,10 @@ int launch_fma(const float* q, const float* kc, const float* vc, const int* lens
     if (e != cudaSuccess) return b2a_host::cuda_fail(e, "cudaFuncSetAttribute(decode_fma)");
   }
   dim3 grid(n_splits, KV, B);
-  kern<<<grid, kFmaWarps * 32, smem, st>>>(q, kc, vc, lens, po, pml, H, KV, group, seq_stride,
-                                           split_rows, n_splits, qscale);
+  const cudaError_t e = b2a_host::launch(kern, grid, dim3(kFmaWarps * 32), smem, st, q, kc, vc,
+                                         lens, po, pml, H, KV, group, seq_stride, split_rows,
+                                         n_splits, qscale);
+  if (e != cudaSuccess) return b2a_host::cuda_fail(e, "decode_fma launch");
   return B2A_OK;
 }
 
@@ -716,9 +736,10 @@ int b2a_decode(const float* q, const void* k_cache, const void* v_cache, const i
   }
   const int smem = ns * static_cast<int>(sizeof(float));
   if (smem > 48 * 1024) return fail(B2A_ERR_UNSUPPORTED, "decode: %d splits exceed the combine limit", ns);
-  decode_combine_kernel<<<B * H, kCombineThreads, smem, st>>>(part_o, part_ml, lens_dev, out,
-                                                              lse_out, H, D, split_rows, ns, max_len);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = b2a_host::launch(decode_combine_kernel, dim3(B * H), dim3(kCombineThreads), smem,
+                                   st, part_o, part_ml, lens_dev, out, lse_out, H, D, split_rows,
+                                   ns, max_len);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "decode launch");
   return B2A_OK;
 }
@@ -732,9 +753,10 @@ int b2a_lse_combine(const float* o_parts, long long o_part_stride, const float* 
   if (lse_part_stride == 0) lse_part_stride = rows;
   if (o_part_stride < static_cast<long long>(rows) * D || lse_part_stride < rows)
     return fail(B2A_ERR_SHAPE, "lse_combine: part strides overlap the parts");
-  lse_combine_kernel<<<rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      o_parts, o_part_stride, lse_parts, lse_part_stride, G, rows, D, out, lse_out);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = b2a_host::launch(lse_combine_kernel, dim3(rows), dim3(128), 0,
+                                   static_cast<cudaStream_t>(stream), o_parts, o_part_stride,
+                                   lse_parts, lse_part_stride, G, rows, D, out, lse_out);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "lse_combine launch");
   return B2A_OK;
 }

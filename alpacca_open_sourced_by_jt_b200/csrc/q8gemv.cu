@@ -23,7 +23,7 @@
 // order (row 0, row 8, row 1, row 9, ...).  A warp streams its tiles with
 // 16-byte loads, sixteen tiles in flight; rows longer than a few hundred
 // blocks are split across the warps of a CTA and meet in shared memory.
-// x is staged once per CTA, applying the step's prologue:
+// x is staged once per CTA from float4 loads, applying the step's prologue:
 //   RMSNORM  x * (1 / sqrt(x.x / n + eps)) * w   (tensor.py:349-356)
 //   SWIGLU   gate / (1 + exp(-gate)) * up          (model.py:1466-1467)
 // and the epilogue stores, adds into out (the residual stream) or, for a
@@ -39,9 +39,8 @@
 namespace b2a {
 namespace q8 {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
 constexpr int kUnroll = 16;  // tiles in flight per warp (a whole task when kw splits rows)
+constexpr int kHold = 2;     // float4 of x held per thread across the RMSNorm reduction
 
 // two codes (bytes sel_lo/sel_hi of a word already biased by +128) -> f16x2
 __device__ __forceinline__ uint32_t codes_f16x2(uint32_t biased, uint32_t sel) {
@@ -50,11 +49,12 @@ __device__ __forceinline__ uint32_t codes_f16x2(uint32_t biased, uint32_t sel) {
   return *reinterpret_cast<const uint32_t*>(&r);
 }
 
-template <int Mode, int Epi>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(
+template <int Mode, int Epi, int kWarps>
+__global__ void __launch_bounds__(kWarps * 32) gemv_kernel(
     const uint4* __restrict__ tiles, const uint32_t* __restrict__ scales, int rows, int cols,
     int kw, const float* __restrict__ x, const float* __restrict__ aux, float eps,
     float* __restrict__ out) {
+  constexpr int kThreads = kWarps * 32;
   extern __shared__ uint4 xs[];  // [nb][8]: B fragments (hi for lanes 0-3, lo for 4-7)
   __shared__ double red[kWarps];
   __shared__ float psum[2][kWarps][16];
@@ -89,17 +89,43 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(
   };
 
   // ---- overlap with the previous kernel: release the next, load weights ---
+  // (and the RMSNorm weight: neither depends on the previous kernel)
+  const int n4 = cols >> 2;
+  const bool held = n4 <= kThreads * kHold;  // x fits in registers: one pass
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  const float4* a4 = reinterpret_cast<const float4*>(aux);
+  float4 av[kHold], xv[kHold];
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (n_tasks > 0) load(static_cast<int>(blockIdx.x) * slots + slot, b_lo);
+  if (Mode == 1 && held) {
+#pragma unroll
+    for (int h = 0; h < kHold; ++h) {
+      const int i = threadIdx.x + h * kThreads;
+      av[h] = i < n4 ? __ldg(a4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- stage x (with the prologue) as f16 hi / lo B fragments -----------------
+  if (held) {
+#pragma unroll
+    for (int h = 0; h < kHold; ++h) {
+      const int i = threadIdx.x + h * kThreads;
+      xv[h] = i < n4 ? __ldg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
   float scale = 1.f;
   if (Mode == 1) {
     double ss = 0.0;
-    for (int i = threadIdx.x; i < cols; i += kThreads) {
-      const double v = x[i];
-      ss += v * v;
+    auto sq = [](float4 v) {
+      return static_cast<double>(v.x) * v.x + static_cast<double>(v.y) * v.y +
+             static_cast<double>(v.z) * v.z + static_cast<double>(v.w) * v.w;
+    };
+    if (held) {
+#pragma unroll
+      for (int h = 0; h < kHold; ++h) ss += sq(xv[h]);
+    } else {
+      for (int i = threadIdx.x; i < n4; i += kThreads) ss += sq(__ldg(x4 + i));
     }
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if (lane == 0) red[warp] = ss;
@@ -109,27 +135,40 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(
     for (int i = 0; i < kWarps; ++i) tot += red[i];
     scale = static_cast<float>(1.0 / sqrt(tot / cols + static_cast<double>(eps)));
   }
-  auto xin = [&](int i) -> float {
-    if (Mode == 2) {
-      const float gt = x[i];
-      return gt / (1.f + expf(-gt)) * x[cols + i];
+  // Four consecutive inputs k..k+3 (k = 4i) land in one word j = (k & 31) >> 3
+  // of the B fragments q0 = (k & 7) / 2 and q0 + 1 of block k / 32: two
+  // 16-bit pairs into the hi entries (lanes q) and two into the lo entries
+  // (lanes 4 + q).  Every input is loaded once, as part of a float4.
+  uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
+  auto put = [&](int i, float4 v, float4 w) {
+    if (Mode == 1) {
+      v = make_float4(v.x * scale * w.x, v.y * scale * w.y, v.z * scale * w.z, v.w * scale * w.w);
+    } else if (Mode == 2) {
+      const float4 u = __ldg(x4 + n4 + i);
+      v = make_float4(v.x / (1.f + expf(-v.x)) * u.x, v.y / (1.f + expf(-v.y)) * u.y,
+                      v.z / (1.f + expf(-v.z)) * u.z, v.w / (1.f + expf(-v.w)) * u.w);
     }
-    const float v = x[i];
-    return Mode == 1 ? v * scale * aux[i] : v;
+    const __half2 h01 = __floats2half2_rn(v.x, v.y), h23 = __floats2half2_rn(v.z, v.w);
+    const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+    const __half2 l01 = __floats2half2_rn(v.x - f01.x, v.y - f01.y);
+    const __half2 l23 = __floats2half2_rn(v.z - f23.x, v.w - f23.y);
+    const int k = i << 2, b = k >> 5, j = (k & 31) >> 3, q0 = (k & 7) >> 1;
+    uint32_t* e = xw + b * 32 + j;  // entry (b, lane) word j at e[lane * 4]
+    e[q0 * 4] = *reinterpret_cast<const uint32_t*>(&h01);
+    e[(q0 + 1) * 4] = *reinterpret_cast<const uint32_t*>(&h23);
+    e[(q0 + 4) * 4] = *reinterpret_cast<const uint32_t*>(&l01);
+    e[(q0 + 5) * 4] = *reinterpret_cast<const uint32_t*>(&l23);
   };
-  for (int i = threadIdx.x; i < nb * 8; i += kThreads) {
-    const int b = i >> 3, e = i & 7, lo = e >> 2, q = e & 3;
-    uint32_t w[4];
+  if (held) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {  // MMA0 b0, MMA0 b1, MMA1 b0, MMA1 b1
-      const int k = 32 * b + (j >> 1) * 16 + (j & 1) * 8 + 2 * q;
-      const float v0 = xin(k), v1 = xin(k + 1);
-      const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-      const __half2 hv = lo ? __floats2half2_rn(v0 - __half2float(h0), v1 - __half2float(h1))
-                            : __halves2half2(h0, h1);
-      w[j] = *reinterpret_cast<const uint32_t*>(&hv);
+    for (int h = 0; h < kHold; ++h) {
+      const int i = threadIdx.x + h * kThreads;
+      if (i < n4) put(i, xv[h], av[h]);
     }
-    xs[i] = make_uint4(w[0], w[1], w[2], w[3]);
+  } else {
+#pragma unroll 4
+    for (int i = threadIdx.x; i < n4; i += kThreads)
+      put(i, __ldg(x4 + i), Mode == 1 ? __ldg(a4 + i) : make_float4(0.f, 0.f, 0.f, 0.f));
   }
   __syncthreads();
 
@@ -212,11 +251,10 @@ __global__ void embed_kernel(const int8_t* __restrict__ codes, const __half* __r
 
 namespace {
 
-template <int Mode, int Epi>
-int launch_gemv(const int8_t* codes, const __half* scales, int rows, int cols, const float* x,
-                const float* aux, float eps, float* out, bool pdl, cudaStream_t st) {
-  namespace Q = b2a::q8;
-  auto kern = Q::gemv_kernel<Mode, Epi>;
+template <int Mode, int Epi, int W>
+int launch_gemv_w(const int8_t* codes, const __half* scales, int rows, int cols, const float* x,
+                  const float* aux, float eps, float* out, bool pdl, cudaStream_t st) {
+  auto kern = b2a::q8::gemv_kernel<Mode, Epi, W>;
   const int smem = cols * 4;  // 8 uint4 B fragments per 32-column block
   if (smem > 48 * 1024) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -227,19 +265,19 @@ int launch_gemv(const int8_t* codes, const __half* scales, int rows, int cols, c
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   // split each row group's blocks over kw warps until there are ~4096 warp
-  // tasks (kw a power of two dividing the CTA's 8 warps, >= 8 blocks each)
+  // tasks (kw a power of two dividing the CTA's W warps, >= 8 blocks each)
   const int rgs = (rows + 15) / 16, nb = cols / 32;
   int kw = 1;
-  while (kw < Q::kWarps && rgs * kw < 4096 && nb / (2 * kw) >= 8) kw *= 2;
-  const int slots = Q::kWarps / kw;
+  while (kw < W && rgs * kw < 4096 && nb / (2 * kw) >= 8) kw *= 2;
+  const int slots = W / kw;
   int grid = (rgs + slots - 1) / slots;
   int per_sm = 1;  // persistent: at most the resident CTAs, each walks its tasks
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Q::kThreads, smem);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, W * 32, smem);
   if (per_sm < 1) per_sm = 1;
   if (grid > sms * per_sm) grid = sms * per_sm;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(Q::kThreads);
+  cfg.blockDim = dim3(W * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -252,6 +290,18 @@ int launch_gemv(const int8_t* codes, const __half* scales, int rows, int cols, c
                                            kw, x, aux, eps, out);
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "q8_gemv launch");
   return B2A_OK;
+}
+
+// Rows of 256+ blocks (8192+ columns) with few row groups run 16-warp CTAs:
+// a 16-way K split gives every warp one round of tiles, so the whole matrix
+// is in flight at once instead of in two register-sized rounds.
+template <int Mode, int Epi>
+int launch_gemv(const int8_t* codes, const __half* scales, int rows, int cols, const float* x,
+                const float* aux, float eps, float* out, bool pdl, cudaStream_t st) {
+  const int rgs = (rows + 15) / 16, nb = cols / 32;
+  if (nb >= 256 && rgs <= 512)
+    return launch_gemv_w<Mode, Epi, 16>(codes, scales, rows, cols, x, aux, eps, out, pdl, st);
+  return launch_gemv_w<Mode, Epi, 8>(codes, scales, rows, cols, x, aux, eps, out, pdl, st);
 }
 
 }  // namespace

@@ -42,9 +42,10 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(
     const int* __restrict__ pos, int tok_seq_mode, TK* __restrict__ k_cache,
     TK* __restrict__ v_cache, long long seq_stride, int n_ctx, TQ* __restrict__ q_out,
     long long qo_tok_stride, int H, int KV, int D, int n_rot, int neox) {
-  // a programmatic dependent launched after this kernel may start its
-  // independent prologue now (it waits for this kernel before reading)
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // No early launch_dependents: a programmatic dependent (the decode) starts
+  // as these short CTAs exit; released at entry it would stream its K/V
+  // rows while the GEMV before this kernel still needs the bandwidth.
+  pdl_wait();  // q/k/v come from the kernel before (a no-op unless PDL-launched)
   const int i = blockIdx.x;
   const int slot = blockIdx.y;
   const int p = pos[i];
@@ -120,6 +121,7 @@ __global__ void __launch_bounds__(kThreads) imrope_append_kernel(
     const int* __restrict__ pos, int tok_seq_mode, TK* __restrict__ k_cache,
     TK* __restrict__ v_cache, long long seq_stride, int n_ctx, TQ* __restrict__ q_out, int H,
     int KV, int D) {
+  pdl_wait();  // q/k/v come from the kernel before (a no-op unless PDL-launched)
   const int i = blockIdx.x;
   const int slot = blockIdx.y;
   const int p = pos[i];
@@ -212,10 +214,10 @@ void launch_rope(dim3 grid, cudaStream_t st, float* q, long long qs, const float
                  const float* ct, const float* stb, int tab_rows, const int* pos, int mode,
                  void* kc, void* vc, long long seq_stride, int n_ctx, void* q_out,
                  long long qos, int H, int KV, int D, int n_rot, int neox) {
-  rope_append_kernel<TK, TQ><<<grid, rope_block(D), 0, st>>>(
-      q, qs, k, ks, v, vs, bq, bk, bv, ct, stb, tab_rows, pos, mode, static_cast<TK*>(kc),
-      static_cast<TK*>(vc), seq_stride, n_ctx, static_cast<TQ*>(q_out), qos, H, KV, D, n_rot,
-      neox);
+  b2a_host::launch(rope_append_kernel<TK, TQ>, grid, dim3(rope_block(D)), 0, st, q, qs, k, ks, v,
+                   vs, bq, bk, bv, ct, stb, tab_rows, pos, mode, static_cast<TK*>(kc),
+                   static_cast<TK*>(vc), seq_stride, n_ctx, static_cast<TQ*>(q_out), qos, H, KV,
+                   D, n_rot, neox);
 }
 
 template <typename TK>
@@ -247,9 +249,9 @@ void launch_imrope(dim3 grid, cudaStream_t st, const float* q, long long qs, con
                    long long ks, const float* v, long long vs, const int* lanes,
                    const ImropeParams& prm, double fscale, const int* pos, int mode, void* kc,
                    void* vc, long long seq_stride, int n_ctx, void* q_out, int H, int KV, int D) {
-  imrope_append_kernel<TK, TQ><<<grid, rope_block(D), 0, st>>>(
-      q, qs, k, ks, v, vs, lanes, prm, fscale, pos, mode, static_cast<TK*>(kc),
-      static_cast<TK*>(vc), seq_stride, n_ctx, static_cast<TQ*>(q_out), H, KV, D);
+  b2a_host::launch(imrope_append_kernel<TK, TQ>, grid, dim3(rope_block(D)), 0, st, q, qs, k, ks,
+                   v, vs, lanes, prm, fscale, pos, mode, static_cast<TK*>(kc),
+                   static_cast<TK*>(vc), seq_stride, n_ctx, static_cast<TQ*>(q_out), H, KV, D);
 }
 
 template <typename TK>

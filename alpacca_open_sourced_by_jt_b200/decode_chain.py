@@ -266,8 +266,14 @@ class DecodeChain:
         for li, ly in enumerate(m.layers):
             ly["wqkv"].gemv(self.x, self.qkv, mode=1, aux=ly["attn_norm"], eps=m.eps,
                             flags=PDL)
-            device.rope_append(q, k, v, pos, self.cos, self.sin, k_cache=self.k_cache[li],
-                               v_cache=self.v_cache[li])
+            # RoPE + append starts while the QKV GEMV drains (programmatic
+            # launch; its position comes from the host copy at the head of
+            # the graph).  The decode and the GEMVs after it measured no
+            # better launched that way: their early starts take bandwidth
+            # from the kernel on the critical path.
+            with device.launch_flags(_lib.LAUNCH_PDL):
+                device.rope_append(q, k, v, pos, self.cos, self.sin, k_cache=self.k_cache[li],
+                                   v_cache=self.v_cache[li])
             device.decode(q, self.k_cache[li], self.v_cache[li], lens, max_len=self.n_ctx,
                           out=self.att, workspace=self._ws, split_rows=self._split)
             ly["wo"].gemv(self.att, self.x, flags=ACCUMULATE | PDL)

@@ -8,6 +8,7 @@ caller supplies `out` and `workspace` buffers (the library never allocates).
 """
 from __future__ import annotations
 
+import contextlib
 import math
 
 import torch
@@ -32,6 +33,21 @@ def _stream(stream=None):
     if stream is None:
         return torch.cuda.current_stream().cuda_stream
     return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+
+
+@contextlib.contextmanager
+def launch_flags(flags: int):
+    """Launch mode of this thread's library calls inside the block
+    (b2a_set_launch_flags).  With LAUNCH_PDL, RoPE + append, decode and the
+    LSE combine start as programmatic dependents of the kernel before them;
+    lengths, positions and the cache rows below each sequence's newest must
+    be complete before that kernel starts (as in a captured decode step)."""
+    lib = _lib.load()
+    old = lib.b2a_set_launch_flags(int(flags))
+    try:
+        yield
+    finally:
+        lib.b2a_set_launch_flags(old)
 
 
 def _need(cond: bool, msg: str):

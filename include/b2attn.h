@@ -68,6 +68,20 @@ const char* b2a_last_error(void);
  * device.  Synchronises the device.  *code = 0 means no kernel reported. */
 int b2a_device_error(int* code, int* aux, int clear);
 
+/* Launch mode of the calling thread's later launches; returns the previous
+ * flags.  B2A_LAUNCH_PDL launches b2a_rope_append, b2a_qwen35_attn_prep's
+ * IMROPE append, b2a_decode (both kernels) and b2a_lse_combine as
+ * programmatic dependents of the kernel before them on the stream: each
+ * starts while that kernel drains and waits for it (griddepcontrol.wait)
+ * before reading what it wrote.  The decode's K/V rows below the newest
+ * (row len - 1 of each sequence) are streamed before that wait, and every
+ * kernel reads lens_dev / positions before it, so those, and the older
+ * cache rows, must be complete before the preceding kernel starts (host
+ * copies or earlier kernels), as in a decode step whose RoPE + append
+ * writes the newest row.  For captured chains of steps; 0 is the default. */
+#define B2A_LAUNCH_PDL 1
+int b2a_set_launch_flags(int flags);
+
 /* ---- (1) split-KV GQA decode ------------------------------------------
  *
  * Replaces Model._attention_np (alpaccaroo/model.py:1231-1252),

@@ -72,3 +72,64 @@ def test_decode_step_rejects_positions_outside_the_cache(cuda_dev):
         step(positions=np.array([-1, 0], np.int32))
     out = step(positions=np.array([0, n_ctx - 1], np.int32))
     assert torch.isfinite(out).all()
+
+
+@pytest.mark.parametrize("dt,D", [(torch.bfloat16, 128), (torch.float16, 64), (torch.float32, 64)])
+def test_programmatic_launches_match_plain(cuda_dev, dt, D):
+    """RoPE + append and the decode launched as programmatic dependents
+    (b2a_set_launch_flags(B2A_LAUNCH_PDL)): the decode streams the rows below
+    each sequence's newest before waiting for the append, so eager calls and
+    a captured graph must give the plain launches' outputs and caches bit for
+    bit.  Lengths 1, 65 (the newest row opens a 64-row tile), 700 and 1024."""
+    from alpacca_open_sourced_by_jt_b200 import _lib, device
+    rng = np.random.default_rng(61)
+    H, KV, n_ctx = 16, 4, 1024
+    lens = np.array([1, 65, 700, 1024], dtype=np.int32)
+    B = len(lens)
+    base_k = torch.from_numpy(rng.standard_normal((B, n_ctx, KV, D), dtype=np.float32)).to(
+        cuda_dev).to(dt)
+    base_v = torch.from_numpy(rng.standard_normal((B, n_ctx, KV, D), dtype=np.float32)).to(
+        cuda_dev).to(dt)
+    ct, st = device.rope_tables(n_ctx, D, 10000.0, device=cuda_dev)
+    q = torch.from_numpy(rng.standard_normal((B, H, D), dtype=np.float32)).to(cuda_dev)
+    k = torch.from_numpy(rng.standard_normal((B, KV, D), dtype=np.float32)).to(cuda_dev)
+    v = torch.from_numpy(rng.standard_normal((B, KV, D), dtype=np.float32)).to(cuda_dev)
+    pos = torch.from_numpy(lens - 1).to(cuda_dev)
+    ln = torch.from_numpy(lens).to(cuda_dev)
+
+    def step(kc, vc, out):
+        qq = q.clone()
+        device.rope_append(qq, k, v, pos, ct, st, k_cache=kc, v_cache=vc, per_sequence=True)
+        device.decode(qq, kc, vc, ln, max_len=n_ctx, out=out)
+        return qq
+
+    kp, vp = base_k.clone(), base_v.clone()
+    want = torch.zeros((B, H, D), device=cuda_dev)
+    step(kp, vp, want)
+    torch.cuda.synchronize()
+    # eager, programmatic
+    ke, ve = base_k.clone(), base_v.clone()
+    got = torch.zeros_like(want)
+    with device.launch_flags(_lib.LAUNCH_PDL):
+        step(ke, ve, got)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    assert torch.equal(ke, kp) and torch.equal(ve, vp)
+    # captured, programmatic (workspace preallocated; no allocation in the capture)
+    kg, vg = base_k.clone(), base_v.clone()
+    gout = torch.zeros_like(want)
+    split = device.decode_split_rows(B, KV, n_ctx, dt)
+    ws = device.decode_workspace(B, H, D, n_ctx, split, cuda_dev)
+    qq = q.clone()
+    s = torch.cuda.Stream(device=cuda_dev)
+    g = torch.cuda.CUDAGraph()
+    with device.launch_flags(_lib.LAUNCH_PDL), torch.cuda.graph(g, stream=s):
+        qq.copy_(q)
+        device.rope_append(qq, k, v, pos, ct, st, k_cache=kg, v_cache=vg, per_sequence=True)
+        device.decode(qq, kg, vg, ln, max_len=n_ctx, out=gout, workspace=ws, split_rows=split)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(gout, want)
+    assert torch.equal(kg, kp) and torch.equal(vg, vp)
+    # the flag is restored on exit
+    assert _lib.load().b2a_set_launch_flags(0) == 0
