@@ -6,6 +6,7 @@
 #include "prefill.cu"
 #include "prefill_pair.cu"
 #include "prefill_head.cu"
+#include "gemm.cu"
 #include "kvconvert.cu"
 #include "qwen35_layer.cu"
 #include "q8gemv.cu"

@@ -1,0 +1,369 @@
+// Dense GEMMs of a device-resident prefill chunk on the 5th-generation tensor
+// cores (tcgen05 + TMEM + TMA), with the chunk's glue fused into the epilogue.
+//
+// The reference runs a chunk's projections as Q8_0 GEMMs over the tokens
+// (Model.forward_batch, alpaccaroo/model.py:1274-1372; the device chain's
+// codes-decoding SIMT GEMM, cuda.py:287-422, called from prefill_chunk,
+// cuda.py:1943-2080).  Here the weights are the 16-bit dequantized copy
+// (d * code, one rounding) and the activations 16-bit, accumulated in fp32:
+//
+//   out[m][n] = sum_k a[m][k] * w[n][k]  (+ c_in[m][n])            STORE
+//   out[m][128g + j] = silu(acc[m][256g + j]) * acc[m][256g + 128 + j]  SWIGLU
+//
+// SWIGLU takes the FFN's gate and up weights interleaved in 128-row groups
+// (gate rows 128g..128g+127, then the matching up rows) and writes the
+// activation the down projection reads (model.py:1352-1354).
+//
+// Kernel: persistent, one CTA per SM, 128 x 256 output tiles taken in
+// m-fastest order (the CTAs working at one time share a weight tile, which
+// then comes from L2).  256 threads:
+//   warp 0       TMA producer: A (128 x 64) and W (256 x 64) K-blocks into a
+//                4-stage ring of 48 KB stages (128-byte swizzle)
+//   warp 1       TMEM owner, single-lane MMA issuer: 4 x tcgen05.mma
+//                (M=128, N=256, K=16) per K-block into one of two 256-column
+//                fp32 accumulators
+//   warps 4-7    epilogue: TMEM -> registers (warp w reads lanes 32(w%4)..,
+//                its 32 rows), residual add / SwiGLU, global store; the other
+//                accumulator takes the next tile's MMAs meanwhile
+// Every wait is a bounded mbarrier wait (B2A_ERR_TIMEOUT on expiry).
+
+namespace b2a {
+namespace gemm {
+
+using prefill::make_idesc;
+using prefill::sw128_desc;
+using prefill::tc_commit;
+using prefill::tc_fence_after;
+using prefill::tc_fence_before;
+using prefill::tc_ld32;
+using prefill::tc_mma;
+using prefill::tc_wait_ld;
+
+constexpr int kBM = 128, kBN = 256, kBK = 64;
+constexpr int kStages = 4;
+constexpr int kThreads = 256;
+constexpr int kABytes = kBM * kBK * 2;  // 16 KB
+constexpr int kWBytes = kBN * kBK * 2;  // 32 KB
+constexpr int kStageBytes = kABytes + kWBytes;
+constexpr int kSmem = kStages * kStageBytes + 1024;
+constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
+
+template <typename TO>
+__device__ __forceinline__ void store32(TO* dst, const float* v);
+template <>
+__device__ __forceinline__ void store32<float>(float* dst, const float* v) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 4)
+    *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+}
+template <>
+__device__ __forceinline__ void store32<__nv_bfloat16>(__nv_bfloat16* dst, const float* v) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    uint4 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __nv_bfloat162 p = __floats2bfloat162_rn(v[i + 2 * j], v[i + 2 * j + 1]);
+      w[j] = *reinterpret_cast<const uint32_t*>(&p);
+    }
+    *reinterpret_cast<uint4*>(dst + i) = u;
+  }
+}
+template <>
+__device__ __forceinline__ void store32<__half>(__half* dst, const float* v) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    uint4 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __half2 p = __floats2half2_rn(v[i + 2 * j], v[i + 2 * j + 1]);
+      w[j] = *reinterpret_cast<const uint32_t*>(&p);
+    }
+    *reinterpret_cast<uint4*>(dst + i) = u;
+  }
+}
+
+template <typename T, typename TO, int Epi>
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
+    const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+    const float* __restrict__ c_in, long long ldc, TO* __restrict__ out, long long ldo, int M,
+    int N, int K) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bar_full[kStages], bar_empty[kStages];
+  __shared__ __align__(8) uint64_t bar_acc_full[2], bar_acc_empty[2];
+  __shared__ uint32_t s_tmem;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = (M + kBM - 1) / kBM, nt = (N + kBN - 1) / kBN;
+  const int n_tiles = mt * nt;
+  const int nk = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bar_full[s], 1);
+      mbar_init(&bar_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar_acc_full[b], 1);
+      mbar_init(&bar_acc_empty[b], 4);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s_tmem)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  // a programmatic dependent may start its prologue; the inputs of this
+  // kernel come from the kernel before, so every role waits for it first
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------ TMA producer -------------------------
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmW);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x) {
+        const int m0 = (t % mt) * kBM, n0 = (t / mt) * kBN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kStages;
+          if (it >= kStages &&
+              !mbar_wait(&bar_empty[s], ((it / kStages) & 1) ^ 1, 0x31000 | (kb & 0xfff))) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bar_full[s], kStageBytes);
+          uint8_t* sa = smem + s * kStageBytes;
+          asm volatile(
+              "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+              " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(sa)),
+              "l"(reinterpret_cast<uint64_t>(&tmA)), "r"(kb * kBK), "r"(m0),
+              "r"(smem_u32(&bar_full[s]))
+              : "memory");
+          asm volatile(
+              "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+              " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(sa + kABytes)),
+              "l"(reinterpret_cast<uint64_t>(&tmW)), "r"(kb * kBK), "r"(n0),
+              "r"(smem_u32(&bar_full[s]))
+              : "memory");
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------ MMA issuer ---------------------------
+      constexpr uint32_t idesc = make_idesc<T>(kBM, kBN, false, false);
+      const uint64_t dA0 = sw128_desc(smem_u32(smem), 16, 1024);
+      const uint64_t dW0 = sw128_desc(smem_u32(smem + kABytes), 16, 1024);
+      constexpr uint64_t kStageStep = kStageBytes >> 4;
+      uint32_t it = 0, tc = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++tc) {
+        const uint32_t b = tc & 1;
+        // the epilogue has drained this accumulator (two tiles ago)
+        if (tc >= 2 && !mbar_wait(&bar_acc_empty[b], ((tc >> 1) - 1) & 1, 0x32000 | (tc & 0xfff))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem + b * kBN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kStages;
+          if (!mbar_wait(&bar_full[s], (it / kStages) & 1, 0x33000 | (kb & 0xfff))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = dA0 + s * kStageStep, dw = dW0 + s * kStageStep;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)  // 32 bytes of K per MMA inside the swizzle atom
+            tc_mma(acc, da + ((kk * 32) >> 4), dw + ((kk * 32) >> 4), idesc, (kb | kk) != 0);
+          tc_commit(&bar_empty[s]);
+        }
+        if (ok) tc_commit(&bar_acc_full[b]);
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------ epilogue --------------------------------
+    const int q = warp & 3;
+    const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    uint32_t tc = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tc) {
+      const uint32_t b = tc & 1;
+      const bool w = __all_sync(0xffffffffu,
+                                mbar_wait(&bar_acc_full[b], (tc >> 1) & 1, 0x34000 | (tc & 0xfff)));
+      if (!w) break;
+      tc_fence_after();
+      const int m0 = (t % mt) * kBM, n0 = (t / mt) * kBN;
+      const int row = m0 + q * 32 + lane;
+      const bool rv = row < M;
+      const uint32_t acc = tl + b * kBN;
+      if (Epi == 0) {
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          float v[32];
+          tc_ld32(acc + c * 32, v);
+          tc_wait_ld();
+          const int col = n0 + c * 32;
+          if (rv && col < N) {
+            if (col + 32 <= N) {
+              if (c_in) {
+                const float* cr = c_in + static_cast<size_t>(row) * ldc + col;
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                  const float4 r = *reinterpret_cast<const float4*>(cr + i);
+                  v[i] += r.x;
+                  v[i + 1] += r.y;
+                  v[i + 2] += r.z;
+                  v[i + 3] += r.w;
+                }
+              }
+              store32<TO>(out + static_cast<size_t>(row) * ldo + col, v);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                if (col + i < N) {
+                  float x = v[i];
+                  if (c_in) x += c_in[static_cast<size_t>(row) * ldc + col + i];
+                  st_elem(out + static_cast<size_t>(row) * ldo + col + i, x);
+                }
+              }
+            }
+          }
+        }
+      } else {
+        // SwiGLU: columns [0,128) of the tile are gate rows, [128,256) the up rows
+#pragma unroll 1
+        for (int c = 0; c < kBN / 64; ++c) {
+          float g[32], u[32];
+          tc_ld32(acc + c * 32, g);
+          tc_ld32(acc + 128 + c * 32, u);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) g[i] = g[i] / (1.f + expf(-g[i])) * u[i];
+          const int col = n0 / 2 + c * 32;
+          if (rv) store32<TO>(out + static_cast<size_t>(row) * ldo + col, g);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_acc_empty[b]);
+    }
+  }
+  // ------------------------------ teardown -----------------------------------
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols));
+  }
+}
+
+}  // namespace gemm
+}  // namespace b2a
+
+// ===========================================================================
+// Host side
+// ===========================================================================
+namespace {
+
+template <typename T, typename TO, int Epi>
+int launch_gemm(const void* a, long long lda, const void* w, long long ldw, const float* c_in,
+                long long ldc, void* out, long long ldo, int M, int N, int K, cudaStream_t st) {
+  namespace G = b2a::gemm;
+  auto kern = G::gemm_kernel<T, TO, Epi>;
+  const CUtensorMapDataType tdt = std::is_same<T, __nv_bfloat16>::value
+                                      ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ta, tw;
+  const uint64_t adims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+  const uint64_t astr[1] = {static_cast<uint64_t>(lda) * 2};
+  const uint64_t wdims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
+  const uint64_t wstr[1] = {static_cast<uint64_t>(ldw) * 2};
+  const uint32_t abox[2] = {static_cast<uint32_t>(G::kBK), static_cast<uint32_t>(G::kBM)};
+  const uint32_t wbox[2] = {static_cast<uint32_t>(G::kBK), static_cast<uint32_t>(G::kBN)};
+  int rc = b2a_host::make_tmap(&ta, tdt, 2, const_cast<void*>(a), adims, astr, abox,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = b2a_host::make_tmap(&tw, tdt, 2, const_cast<void*>(w), wdims, wstr, wbox,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
+  if (e != cudaSuccess) return b2a_host::cuda_fail(e, "cudaFuncSetAttribute(gemm)");
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int tiles = ((M + G::kBM - 1) / G::kBM) * ((N + G::kBN - 1) / G::kBN);
+  const int grid = tiles < sms ? tiles : sms;
+  e = b2a_host::launch(kern, dim3(grid), dim3(G::kThreads), G::kSmem, st, ta, tw, c_in, ldc,
+                       static_cast<TO*>(out), ldo, M, N, K);
+  if (e != cudaSuccess) return b2a_host::cuda_fail(e, "gemm launch");
+  return B2A_OK;
+}
+
+template <typename T, int Epi>
+int gemm_out(int out_dtype, const void* a, long long lda, const void* w, long long ldw,
+             const float* c_in, long long ldc, void* out, long long ldo, int M, int N, int K,
+             cudaStream_t st) {
+  switch (out_dtype) {
+    case B2A_F32:
+      return launch_gemm<T, float, Epi>(a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
+    case B2A_F16:
+      return launch_gemm<T, __half, Epi>(a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
+    case B2A_BF16:
+      return launch_gemm<T, __nv_bfloat16, Epi>(a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
+  }
+  return b2a_host::fail(B2A_ERR_DTYPE, "gemm: out_dtype %d", out_dtype);
+}
+
+}  // namespace
+
+extern "C" {
+
+int b2a_gemm(const void* a, long long lda, const void* w, long long ldw, int dtype,
+             const float* c_in, long long ldc, void* out, long long ldo, int out_dtype, int M,
+             int N, int K, int epilogue, void* stream) {
+  using b2a_host::fail;
+  if (!a || !w || !out) return fail(B2A_ERR_ARG, "gemm: null pointer argument");
+  if (M <= 0 || N <= 0 || K <= 0) return fail(B2A_ERR_SHAPE, "gemm: M=%d N=%d K=%d", M, N, K);
+  if (lda < K || ldw < K || (lda & 7) || (ldw & 7))
+    return fail(B2A_ERR_ALIGN, "gemm: lda/ldw must be >= K and multiples of 8 elements");
+  if (!b2a_host::aligned16(a) || !b2a_host::aligned16(w) || !b2a_host::aligned16(out) ||
+      (c_in && !b2a_host::aligned16(c_in)))
+    return fail(B2A_ERR_ALIGN, "gemm: a, w, c_in and out must be 16-byte aligned");
+  if (epilogue != B2A_GEMM_STORE && epilogue != B2A_GEMM_SWIGLU)
+    return fail(B2A_ERR_ARG, "gemm: epilogue %d", epilogue);
+  const int out_cols = epilogue == B2A_GEMM_SWIGLU ? N / 2 : N;
+  if (ldo < out_cols || (c_in && ldc < N))
+    return fail(B2A_ERR_SHAPE, "gemm: ldo/ldc smaller than the row");
+  const int eb = b2a_host::elem_size(out_dtype);
+  if (eb == 0) return fail(B2A_ERR_DTYPE, "gemm: out_dtype %d", out_dtype);
+  if ((ldo * eb) % 16 || (c_in && (ldc % 4)))
+    return fail(B2A_ERR_ALIGN, "gemm: output and c_in rows must start on 16-byte boundaries");
+  if (epilogue == B2A_GEMM_SWIGLU && (N % 256 || c_in))
+    return fail(B2A_ERR_SHAPE, "gemm: SWIGLU needs N a multiple of 256 and no c_in");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == B2A_BF16)
+    return epilogue == B2A_GEMM_SWIGLU
+               ? gemm_out<__nv_bfloat16, 1>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st)
+               : gemm_out<__nv_bfloat16, 0>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
+  if (dtype == B2A_F16)
+    return epilogue == B2A_GEMM_SWIGLU
+               ? gemm_out<__half, 1>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st)
+               : gemm_out<__half, 0>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
+  return fail(B2A_ERR_DTYPE, "gemm: operand dtype %d (f16 or bf16)", dtype);
+}
+
+}  // extern "C"

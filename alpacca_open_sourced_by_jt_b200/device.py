@@ -278,3 +278,33 @@ def imrope_append(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, lanes: torc
         k_cache.stride(0), n_ctx, _code(k_cache.dtype), _ptr(q_out), _code(q_out.dtype), n, H,
         KV, D, _stream(stream)))
     return q_out
+
+
+GEMM_STORE, GEMM_SWIGLU = 0, 1
+
+
+def gemm(a: torch.Tensor, w: torch.Tensor, *, out=None, out_dtype=torch.float32, c_in=None,
+         epilogue: int = GEMM_STORE, stream=None) -> torch.Tensor:
+    """out = a . w^T (+ c_in) on the tcgen05 tensor cores (b2a_gemm).
+
+    a (M, K) and w (N, K) 16-bit with unit stride along K; c_in f32 (M, N)
+    or None (may be out itself, for an in-place residual add).  With
+    GEMM_SWIGLU, w's rows come in 256-row groups of 128 gate rows and the
+    matching 128 up rows and out is silu(gate) * up, (M, N / 2)."""
+    _need(a.dim() == 2 and w.dim() == 2 and a.shape[1] == w.shape[1], "a (M,K), w (N,K)")
+    _need(a.dtype == w.dtype and a.dtype in (torch.float16, torch.bfloat16), "16-bit a and w")
+    _need(a.stride(1) == 1 and w.stride(1) == 1, "a and w need unit stride along K")
+    M, K = a.shape
+    N = w.shape[0]
+    cols = N // 2 if epilogue == GEMM_SWIGLU else N
+    if out is None:
+        out = torch.empty((M, cols), dtype=out_dtype, device=a.device)
+    _need(out.dim() == 2 and out.shape == (M, cols) and out.stride(1) == 1, "out (M, cols)")
+    if c_in is not None:
+        _need(c_in.dtype == torch.float32 and c_in.shape == (M, N) and c_in.stride(1) == 1,
+              "c_in f32 (M, N)")
+    _lib.check(_lib.load().b2a_gemm(
+        _ptr(a), a.stride(0), _ptr(w), w.stride(0), _code(a.dtype), _ptr(c_in),
+        0 if c_in is None else c_in.stride(0), _ptr(out), out.stride(0), _code(out.dtype), M, N,
+        K, int(epilogue), _stream(stream)))
+    return out

@@ -13,21 +13,18 @@ straight into a DecodeChain's caches, so decoding continues from it:
   embed rows              b2a_q8_embed (all T tokens)
   per layer:
     h    = RMSNorm(x)      b2a_rmsnorm_rows, written as the cache's 16-bit type
-    qkv  = h . Wqkv^T      tensor-core GEMM, f32 out
+    qkv  = h . Wqkv^T      b2a_gemm (tcgen05), f32 out
     RoPE + K/V append, q rotated to 16 bits           b2a_rope_append
     att  = causal prefill over cache rows 0..pos0+T-1  b2a_prefill (tcgen05)
-    x   += att . Wo^T      tensor-core GEMM with the residual as its C input
+    x   += att . Wo^T      b2a_gemm, the residual added in its epilogue, in place
     h    = RMSNorm(x)      b2a_rmsnorm_rows
-    gu   = h . Wgu^T       ([gate rows; up rows])
-    act  = SwiGLU(gu)      b2a_swiglu_rows
-    x   += act . Wdown^T
+    act  = SwiGLU(h . Wgu^T)  b2a_gemm with the SwiGLU epilogue, 16-bit out
+    x   += act . Wdown^T   b2a_gemm, residual in the epilogue
   logits = Woutput . RMSNorm(x[T-1])   b2a_q8_gemv (the decode path's Q8_0 GEMV)
 
-The GEMMs are plain dense products, so they run through cuBLAS on the
-16-bit dequantized weights (d * code, one copy per matrix made at set-up)
-with f32 accumulation and f32 output; everything fused around them is this
-library's own kernels.  The 16-bit operands are the one precision step away
-from the reference's f32 SIMT GEMM.
+The GEMMs run on 16-bit dequantized weights (d * code, one copy per matrix
+made at set-up) with fp32 accumulation.  The 16-bit operands are the one
+precision step away from the reference's f32 SIMT GEMM.
 """
 from __future__ import annotations
 
@@ -58,12 +55,15 @@ class ChunkPrefill:
         self.dt, self.code = dt, device._code(dt)
         dev = m.device
         self.max_chunk = int(max_chunk)
+        if m.F % 128:
+            raise _lib.B2AShapeError(_lib.ERR_SHAPE, "chunk prefill needs n_ff % 128 == 0")
         self.w = [dict(qkv=_dequant(ly["wqkv"], dt), wo=_dequant(ly["wo"], dt),
                        gu=self._gate_up(_dequant(ly["wgu"], dt), m.F),
                        down=_dequant(ly["w_down"], dt))
                   for ly in m.layers]
         T, E, H, KV, D, F = self.max_chunk, m.E, m.H, m.KV, m.D, m.F
         self.x = torch.zeros((T, E), dtype=torch.float32, device=dev)
+        self.qkv = torch.zeros((T, (H + 2 * KV) * D), dtype=torch.float32, device=dev)
         self.h = torch.zeros((T, E), dtype=dt, device=dev)
         self.qrot = torch.zeros((T, H, D), dtype=dt, device=dev)
         self.att = torch.zeros((T, H, D), dtype=dt, device=dev)
@@ -75,9 +75,12 @@ class ChunkPrefill:
     @staticmethod
     def _gate_up(w: torch.Tensor, F: int) -> torch.Tensor:
         """The decode path's gate/up matrix (8 gate rows, 8 up rows, ...) as
-        [all gate rows; all up rows] for the chunk GEMM."""
+        the GEMM's SwiGLU layout: 128 gate rows, then the matching 128 up
+        rows, for each 128 features."""
         g = w.view(F // 8, 2, 8, -1)
-        return torch.cat([g[:, 0].reshape(F, -1), g[:, 1].reshape(F, -1)]).contiguous()
+        gate, up = g[:, 0].reshape(F, -1), g[:, 1].reshape(F, -1)
+        return torch.stack([gate.view(F // 128, 128, -1), up.view(F // 128, 128, -1)],
+                           1).reshape(2 * F, -1).contiguous()
 
     def _norm(self, x, w, T):
         m = self.m
@@ -111,7 +114,7 @@ class ChunkPrefill:
         t_kv = pos0 + T
         for li, (ly, w) in enumerate(zip(m.layers, self.w)):
             h = self._norm(x, ly["attn_norm"], T)
-            qkv = torch.mm(h, w["qkv"].t(), out_dtype=torch.float32)
+            qkv = device.gemm(h, w["qkv"], out=self.qkv[:T])
             q = qkv[:, :qd].view(T, H, D)
             k = qkv[:, qd:qd + kd].view(T, KV, D)
             v = qkv[:, qd + kd:].view(T, KV, D)
@@ -119,12 +122,10 @@ class ChunkPrefill:
                                v_cache=ch.v_cache[li], q_out=self.qrot[:T])
             att = device.prefill(self.qrot[:T], ch.k_cache[li][0, :t_kv],
                                  ch.v_cache[li][0, :t_kv], pos, out=self.att[:T])
-            x.copy_(torch.addmm(x, att.view(T, qd), w["wo"].t(), out_dtype=torch.float32))
+            device.gemm(att.view(T, qd), w["wo"], out=x, c_in=x)
             h = self._norm(x, ly["ffn_norm"], T)
-            gu = torch.mm(h, w["gu"].t(), out_dtype=torch.float32)
-            _lib.check(lib.b2a_swiglu_rows(gu.data_ptr(), 2 * m.F, 0, self.act.data_ptr(), m.F,
-                                           self.code, T, m.F, st))
-            x.copy_(torch.addmm(x, self.act[:T], w["down"].t(), out_dtype=torch.float32))
+            device.gemm(h, w["gu"], out=self.act[:T], epilogue=device.GEMM_SWIGLU)
+            device.gemm(self.act[:T], w["down"], out=x, c_in=x)
         if not want_logits:
             return None
         m.output.gemv(x[T - 1], self.logits, mode=1, aux=m.out_norm, eps=m.eps, flags=PDL)

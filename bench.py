@@ -541,9 +541,9 @@ def bench_prefill_chunk(dev, steps, warmup):
                          "unit": "TFLOP/s", "frac": round(tf / bf16, 4),
                          "peak_source": f"{src} (MEASURED_PEAKS.json bf16_tflops, burst)"},
             "config": "16 layers, hidden 2048, 32/8 heads x 64, FFN 8192, vocab 128256; "
-                      "weights dequantized to f16 for the GEMMs (cuBLAS, f32 out), RMSNorm / "
-                      "RoPE+append / tcgen05 causal prefill / SwiGLU kernels of this library; "
-                      "eager launches (about 10 per layer)"}
+                      "weights dequantized to f16; every kernel this library's: tcgen05 GEMMs "
+                      "(residual add and SwiGLU in their epilogues), RMSNorm, RoPE+append, "
+                      "tcgen05 causal prefill; eager launches (7 per layer)"}
 
 
 def bench_e2e(dev, st, steps, warmup):

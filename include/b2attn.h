@@ -313,6 +313,27 @@ int b2a_rmsnorm_rows(const float* x, long long x_row_stride, const float* w, flo
 int b2a_swiglu_rows(const float* gu, long long gu_row_stride, int interleaved, void* out,
                     long long out_row_stride, int out_dtype, int n_rows, int F, void* stream);
 
+/* ---- prefill-chunk GEMMs on the tcgen05 tensor cores ---------------------
+ *
+ * The dense projections of a device-resident prefill chunk (the reference's
+ * Model.forward_batch, model.py:1274-1372; device prefill_chunk,
+ * cuda.py:1943-2080, whose Q8_0 GEMM is cuda.py:287-422), with 16-bit
+ * operands (the dequantized weights d * code) and fp32 accumulation:
+ *   B2A_GEMM_STORE   out[m][n] = sum_k a[m][k] * w[n][k] (+ c_in[m][n])
+ *   B2A_GEMM_SWIGLU  out[m][128g + j] = silu(s[256g + j]) * s[256g + 128 + j]
+ *                    for s = a . w^T: w's rows come in 256-row groups of 128
+ *                    gate rows then the matching 128 up rows (model.py:
+ *                    1352-1354); out has N / 2 columns, N % 256 == 0, no c_in
+ * a [M][lda] and w [N][ldw] of dtype (B2A_F16 / B2A_BF16), K contiguous;
+ * c_in f32 [M][ldc] or NULL (may equal out for an in-place residual add);
+ * out [M][ldo] of out_dtype.  Pointers 16-byte aligned; lda, ldw multiples of
+ * 8 elements; rows of out and c_in start on 16-byte boundaries. */
+#define B2A_GEMM_STORE 0
+#define B2A_GEMM_SWIGLU 1
+int b2a_gemm(const void* a, long long lda, const void* w, long long ldw, int dtype,
+             const float* c_in, long long ldc, void* out, long long ldo, int out_dtype, int M,
+             int N, int K, int epilogue, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
