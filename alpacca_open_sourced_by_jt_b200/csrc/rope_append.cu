@@ -23,10 +23,12 @@
 
 #include "b2a_common.cuh"
 
+#include <algorithm>
+
 namespace b2a {
 namespace rope {
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;
 constexpr int kMaxPairs = 128;  // head_dim <= 256
 
 // Grid (token, head slot): slots [0, H) are the token's q heads, [H, H+KV)
@@ -41,13 +43,14 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(
     const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int tab_rows,
     const int* __restrict__ pos, int tok_seq_mode, TK* __restrict__ k_cache,
     TK* __restrict__ v_cache, long long seq_stride, int n_ctx, TQ* __restrict__ q_out,
-    long long qo_tok_stride, int H, int KV, int D, int n_rot, int neox) {
+    long long qo_tok_stride, int H, int KV, int D, int n_rot, int neox, int n_tok) {
   // No early launch_dependents: a programmatic dependent (the decode) starts
   // as these short CTAs exit; released at entry it would stream its K/V
   // rows while the GEMV before this kernel still needs the bandwidth.
   pdl_wait();  // q/k/v come from the kernel before (a no-op unless PDL-launched)
-  const int i = blockIdx.x;
+  const int i = blockIdx.x * blockDim.y + threadIdx.y;  // blockDim.y tokens per CTA
   const int slot = blockIdx.y;
+  if (i >= n_tok) return;
   const int p = pos[i];
   if (p < 0 || p >= n_ctx || p >= tab_rows) {
     if (threadIdx.x == 0 && slot == 0) set_dev_error(B2A_ERR_POSITION, i);
@@ -120,10 +123,11 @@ __global__ void __launch_bounds__(kThreads) imrope_append_kernel(
     const int* __restrict__ lanes, const __grid_constant__ ImropeParams prm, double freq_scale,
     const int* __restrict__ pos, int tok_seq_mode, TK* __restrict__ k_cache,
     TK* __restrict__ v_cache, long long seq_stride, int n_ctx, TQ* __restrict__ q_out, int H,
-    int KV, int D) {
+    int KV, int D, int n_tok) {
   pdl_wait();  // q/k/v come from the kernel before (a no-op unless PDL-launched)
-  const int i = blockIdx.x;
+  const int i = blockIdx.x * blockDim.y + threadIdx.y;  // blockDim.y tokens per CTA
   const int slot = blockIdx.y;
+  if (i >= n_tok) return;
   const int p = pos[i];
   if (p < 0 || p >= n_ctx) {
     if (threadIdx.x == 0 && slot == 0) set_dev_error(B2A_ERR_POSITION, i);
@@ -209,34 +213,35 @@ int imrope_lane(int pair, const int* sec) {
 }
 
 template <typename TK, typename TQ>
-void launch_rope(dim3 grid, cudaStream_t st, float* q, long long qs, const float* k, long long ks,
+void launch_rope(dim3 grid, dim3 block, int n_tok, cudaStream_t st, float* q, long long qs,
+                 const float* k, long long ks,
                  const float* v, long long vs, const float* bq, const float* bk, const float* bv,
                  const float* ct, const float* stb, int tab_rows, const int* pos, int mode,
                  void* kc, void* vc, long long seq_stride, int n_ctx, void* q_out,
                  long long qos, int H, int KV, int D, int n_rot, int neox) {
-  b2a_host::launch(rope_append_kernel<TK, TQ>, grid, dim3(rope_block(D)), 0, st, q, qs, k, ks, v,
-                   vs, bq, bk, bv, ct, stb, tab_rows, pos, mode, static_cast<TK*>(kc),
-                   static_cast<TK*>(vc), seq_stride, n_ctx, static_cast<TQ*>(q_out), qos, H, KV,
-                   D, n_rot, neox);
+  b2a_host::launch(rope_append_kernel<TK, TQ>, grid, block, 0, st, q, qs, k, ks, v, vs, bq, bk,
+                   bv, ct, stb, tab_rows, pos, mode, static_cast<TK*>(kc), static_cast<TK*>(vc),
+                   seq_stride, n_ctx, static_cast<TQ*>(q_out), qos, H, KV, D, n_rot, neox, n_tok);
 }
 
 template <typename TK>
-int rope_qdt(int q_dtype, dim3 grid, cudaStream_t st, float* q, long long qs, const float* k,
+int rope_qdt(int q_dtype, dim3 grid, dim3 block, int n_tok, cudaStream_t st, float* q,
+             long long qs, const float* k,
              long long ks, const float* v, long long vs, const float* bq, const float* bk,
              const float* bv, const float* ct, const float* stb, int tab_rows, const int* pos,
              int mode, void* kc, void* vc, long long seq_stride, int n_ctx, void* q_out,
              long long qos, int H, int KV, int D, int n_rot, int neox) {
   switch (q_dtype) {
     case B2A_F32:
-      launch_rope<TK, float>(grid, st, q, qs, k, ks, v, vs, bq, bk, bv, ct, stb, tab_rows, pos,
+      launch_rope<TK, float>(grid, block, n_tok, st, q, qs, k, ks, v, vs, bq, bk, bv, ct, stb, tab_rows, pos,
                              mode, kc, vc, seq_stride, n_ctx, q_out, qos, H, KV, D, n_rot, neox);
       return B2A_OK;
     case B2A_F16:
-      launch_rope<TK, __half>(grid, st, q, qs, k, ks, v, vs, bq, bk, bv, ct, stb, tab_rows, pos,
+      launch_rope<TK, __half>(grid, block, n_tok, st, q, qs, k, ks, v, vs, bq, bk, bv, ct, stb, tab_rows, pos,
                               mode, kc, vc, seq_stride, n_ctx, q_out, qos, H, KV, D, n_rot, neox);
       return B2A_OK;
     case B2A_BF16:
-      launch_rope<TK, __nv_bfloat16>(grid, st, q, qs, k, ks, v, vs, bq, bk, bv, ct, stb, tab_rows,
+      launch_rope<TK, __nv_bfloat16>(grid, block, n_tok, st, q, qs, k, ks, v, vs, bq, bk, bv, ct, stb, tab_rows,
                                      pos, mode, kc, vc, seq_stride, n_ctx, q_out, qos, H, KV, D,
                                      n_rot, neox);
       return B2A_OK;
@@ -245,31 +250,33 @@ int rope_qdt(int q_dtype, dim3 grid, cudaStream_t st, float* q, long long qs, co
 }
 
 template <typename TK, typename TQ>
-void launch_imrope(dim3 grid, cudaStream_t st, const float* q, long long qs, const float* k,
+void launch_imrope(dim3 grid, dim3 block, int n_tok, cudaStream_t st, const float* q,
+                   long long qs, const float* k,
                    long long ks, const float* v, long long vs, const int* lanes,
                    const ImropeParams& prm, double fscale, const int* pos, int mode, void* kc,
                    void* vc, long long seq_stride, int n_ctx, void* q_out, int H, int KV, int D) {
-  b2a_host::launch(imrope_append_kernel<TK, TQ>, grid, dim3(rope_block(D)), 0, st, q, qs, k, ks,
-                   v, vs, lanes, prm, fscale, pos, mode, static_cast<TK*>(kc),
-                   static_cast<TK*>(vc), seq_stride, n_ctx, static_cast<TQ*>(q_out), H, KV, D);
+  b2a_host::launch(imrope_append_kernel<TK, TQ>, grid, block, 0, st, q, qs, k, ks, v, vs, lanes,
+                   prm, fscale, pos, mode, static_cast<TK*>(kc), static_cast<TK*>(vc),
+                   seq_stride, n_ctx, static_cast<TQ*>(q_out), H, KV, D, n_tok);
 }
 
 template <typename TK>
-int imrope_qdt(int q_dtype, dim3 grid, cudaStream_t st, const float* q, long long qs,
+int imrope_qdt(int q_dtype, dim3 grid, dim3 block, int n_tok, cudaStream_t st, const float* q,
+               long long qs,
                const float* k, long long ks, const float* v, long long vs, const int* lanes,
                const ImropeParams& prm, double fscale, const int* pos, int mode, void* kc,
                void* vc, long long seq_stride, int n_ctx, void* q_out, int H, int KV, int D) {
   switch (q_dtype) {
     case B2A_F32:
-      launch_imrope<TK, float>(grid, st, q, qs, k, ks, v, vs, lanes, prm, fscale, pos, mode, kc,
+      launch_imrope<TK, float>(grid, block, n_tok, st, q, qs, k, ks, v, vs, lanes, prm, fscale, pos, mode, kc,
                                vc, seq_stride, n_ctx, q_out, H, KV, D);
       return B2A_OK;
     case B2A_F16:
-      launch_imrope<TK, __half>(grid, st, q, qs, k, ks, v, vs, lanes, prm, fscale, pos, mode, kc,
+      launch_imrope<TK, __half>(grid, block, n_tok, st, q, qs, k, ks, v, vs, lanes, prm, fscale, pos, mode, kc,
                                 vc, seq_stride, n_ctx, q_out, H, KV, D);
       return B2A_OK;
     case B2A_BF16:
-      launch_imrope<TK, __nv_bfloat16>(grid, st, q, qs, k, ks, v, vs, lanes, prm, fscale, pos,
+      launch_imrope<TK, __nv_bfloat16>(grid, block, n_tok, st, q, qs, k, ks, v, vs, lanes, prm, fscale, pos,
                                        mode, kc, vc, seq_stride, n_ctx, q_out, H, KV, D);
       return B2A_OK;
   }
@@ -317,22 +324,24 @@ int b2a_rope_append(float* q, long long q_tok_stride, const float* k, long long 
   }
   if (n_tok == 0) return B2A_OK;
   if (D & 1) return fail(B2A_ERR_SHAPE, "rope_append: head_dim %d must be even", D);
-  dim3 grid(n_tok, H + 2 * KV);
+  // tokens per CTA: one for a decode step, up to 8 for a prefill chunk
+  const int tpb = rope_block(D), ty = std::max(1, std::min({8, n_tok, R::kThreads / tpb}));
+  dim3 grid((n_tok + ty - 1) / ty, H + 2 * KV), block(tpb, ty);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int neox = style == B2A_ROPE_NEOX;
   switch (kv_dtype) {
     case B2A_F32:
-      rc = rope_qdt<float>(q_out_dtype, grid, st, q, q_tok_stride, k, k_tok_stride, v, v_tok_stride,
+      rc = rope_qdt<float>(q_out_dtype, grid, block, n_tok, st, q, q_tok_stride, k, k_tok_stride, v, v_tok_stride,
                            bq, bk, bv, cos_tab, sin_tab, tab_rows, pos_dev, tok_seq_mode, k_cache,
                            v_cache, seq_stride, n_ctx, q_out, qos, H, KV, D, n_rot, neox);
       break;
     case B2A_F16:
-      rc = rope_qdt<__half>(q_out_dtype, grid, st, q, q_tok_stride, k, k_tok_stride, v, v_tok_stride,
+      rc = rope_qdt<__half>(q_out_dtype, grid, block, n_tok, st, q, q_tok_stride, k, k_tok_stride, v, v_tok_stride,
                             bq, bk, bv, cos_tab, sin_tab, tab_rows, pos_dev, tok_seq_mode, k_cache,
                             v_cache, seq_stride, n_ctx, q_out, qos, H, KV, D, n_rot, neox);
       break;
     case B2A_BF16:
-      rc = rope_qdt<__nv_bfloat16>(q_out_dtype, grid, st, q, q_tok_stride, k, k_tok_stride, v,
+      rc = rope_qdt<__nv_bfloat16>(q_out_dtype, grid, block, n_tok, st, q, q_tok_stride, k, k_tok_stride, v,
                                    v_tok_stride, bq, bk, bv, cos_tab, sin_tab, tab_rows, pos_dev,
                                    tok_seq_mode, k_cache, v_cache, seq_stride, n_ctx, q_out, qos, H,
                                    KV, D, n_rot, neox);
@@ -372,21 +381,23 @@ int b2a_imrope_append(const float* q, long long q_tok_stride, const float* k,
   }
   if (n_tok == 0) return B2A_OK;
   if (D & 1) return fail(B2A_ERR_SHAPE, "imrope_append: head_dim %d must be even", D);
-  dim3 grid(n_tok, H + 2 * KV);
+  // tokens per CTA: one for a decode step, up to 8 for a prefill chunk
+  const int tpb = rope_block(D), ty = std::max(1, std::min({8, n_tok, R::kThreads / tpb}));
+  dim3 grid((n_tok + ty - 1) / ty, H + 2 * KV), block(tpb, ty);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (kv_dtype) {
     case B2A_F32:
-      rc = imrope_qdt<float>(q_out_dtype, grid, st, q, q_tok_stride, k, k_tok_stride, v,
+      rc = imrope_qdt<float>(q_out_dtype, grid, block, n_tok, st, q, q_tok_stride, k, k_tok_stride, v,
                              v_tok_stride, lanes_dev, prm, freq_scale, pos_dev, tok_seq_mode,
                              k_cache, v_cache, seq_stride, n_ctx, q_out, H, KV, D);
       break;
     case B2A_F16:
-      rc = imrope_qdt<__half>(q_out_dtype, grid, st, q, q_tok_stride, k, k_tok_stride, v,
+      rc = imrope_qdt<__half>(q_out_dtype, grid, block, n_tok, st, q, q_tok_stride, k, k_tok_stride, v,
                               v_tok_stride, lanes_dev, prm, freq_scale, pos_dev, tok_seq_mode,
                               k_cache, v_cache, seq_stride, n_ctx, q_out, H, KV, D);
       break;
     case B2A_BF16:
-      rc = imrope_qdt<__nv_bfloat16>(q_out_dtype, grid, st, q, q_tok_stride, k, k_tok_stride, v,
+      rc = imrope_qdt<__nv_bfloat16>(q_out_dtype, grid, block, n_tok, st, q, q_tok_stride, k, k_tok_stride, v,
                                      v_tok_stride, lanes_dev, prm, freq_scale, pos_dev,
                                      tok_seq_mode, k_cache, v_cache, seq_stride, n_ctx, q_out, H,
                                      KV, D);
