@@ -25,6 +25,8 @@ Also reported on the same line:
             llama decoder as one CUDA graph, tokens/s (device and e2e)
   prefill_chunk  a 2048-token prefill chunk of the same model kept on the
             device, tokens/s and TFLOP/s
+  gemm      the chunk's four projections (tcgen05 b2a_gemm with the chunk's
+            epilogues) at those shapes, TFLOP/s, with cuBLAS beside each
   e2e       the decode step through the public API with host buffers
             (DecodeStep, one CUDA graph per token): per step the pinned host
             q/k/v rows and positions go H2D, the fused RoPE+append writes
@@ -36,8 +38,8 @@ Also reported on the same line:
 Multi-GPU (torchrun, one rank per GPU): every rank decodes its own batch of
 16 sequences (sequence sharding, no collective on the data path), so
 scaling is weak; timing is the max over ranks of CUDA-event time.  The
-single-GPU legs (kvstate, qwen35_layer, decode_step, prefill_chunk) run
-only when the job has one GPU.
+single-GPU legs (kvstate, qwen35_layer, decode_step, prefill_chunk, gemm)
+run only when the job has one GPU.
 
 `--impl reference` times the reference's CPU implementation (the NumPy
 restatement in oracle/, the reference itself being Python that does not
@@ -503,6 +505,65 @@ def bench_decode_step(dev, steps, warmup):
     return res
 
 
+def bench_gemm(dev, steps, warmup):
+    """The prefill chunk's projections (b2a_gemm, tcgen05) at the config-5 shapes for a
+    2048-token chunk, each with the epilogue the chunk uses (QKV fp32 out, Wo and down
+    with the residual added in place, gate/up with SwiGLU writing f16), timed by CUDA
+    events; beside each, PyTorch's 16-bit GEMM with fp32 output (cuBLAS) on the same
+    operands without the fused work.  Bound: tensor cores."""
+    import torch
+    from alpacca_open_sourced_by_jt_b200 import device
+    T, E, F = 2048, C5["n_embd"], C5["n_ff"]
+    qkv_n = (C5["n_head"] + 2 * C5["n_kv"]) * C5["head_dim"]
+    g = torch.Generator(device=dev).manual_seed(7)
+    shapes = (("qkv", qkv_n, E, "store"), ("wo", E, E, "residual"),
+              ("gate_up", 2 * F, E, "swiglu"), ("down", E, F, "residual"))
+    n = max(3, min(steps, 20))
+
+    def timed(fn):
+        for _ in range(max(3, min(warmup, 5))):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n * 1e3  # us
+
+    hbm, bf16, bf16_sus, src = peaks()
+    out, tot_fl, tot_us = {}, 0.0, 0.0
+    for name, N, K, epi in shapes:
+        a = torch.randn((T, K), device=dev, generator=g).to(torch.float16)
+        w = (0.02 * torch.randn((N, K), device=dev, generator=g)).to(torch.float16)
+        if epi == "swiglu":
+            o = torch.empty((T, N // 2), device=dev, dtype=torch.float16)
+            fn = lambda: device.gemm(a, w, out=o, epilogue=device.GEMM_SWIGLU)
+        elif epi == "residual":
+            o = torch.zeros((T, N), device=dev)
+            fn = lambda: device.gemm(a, w, out=o, c_in=o)
+        else:
+            o = torch.empty((T, N), device=dev)
+            fn = lambda: device.gemm(a, w, out=o)
+        us = timed(fn)
+        ref = timed(lambda: torch.mm(a, w.t(), out_dtype=torch.float32))
+        fl = 2.0 * T * N * K
+        tot_fl += fl
+        tot_us += us
+        out[name] = {"M": T, "N": N, "K": K, "epilogue": epi, "us": round(us, 1),
+                     "tflops": round(fl / us / 1e6, 1), "frac": round(fl / us / 1e6 / bf16, 4),
+                     "cublas_tflops_plain": round(fl / ref / 1e6, 1)}
+        del a, w, o
+    tf = tot_fl / tot_us / 1e6
+    return {"metric": "prefill-chunk GEMM TFLOPS (config-5 shapes, 2048 tokens)",
+            "value": round(tf, 1), "unit": "TFLOP/s", "launches": 4 * n,
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": bf16,
+                         "unit": "TFLOP/s", "frac": round(tf / bf16, 4),
+                         "peak_source": f"{src} (MEASURED_PEAKS.json bf16_tflops, burst)"},
+            "shapes": out}
+
+
 def bench_prefill_chunk(dev, steps, warmup):
     """Device-resident prefill chunk (prefill_chain.ChunkPrefill) on the
     config-5 model: one 2048-token chunk at position 0 into an fp16 cache of
@@ -696,6 +757,9 @@ def run_ours(args):
     pch = None
     if world == 1 and args.only in (None, "prefill_chunk"):
         pch = bench_prefill_chunk(dev, args.steps, args.warmup)
+    gmm = None
+    if world == 1 and args.only in (None, "gemm"):
+        gmm = bench_gemm(dev, args.steps, args.warmup)
     ms = st["ms"]
     if dist is not None:
         t = torch.tensor([ms], device=dev)
@@ -749,6 +813,8 @@ def run_ours(args):
             result["decode_step"] = c5
         if pch:
             result["prefill_chunk"] = pch
+        if gmm:
+            result["gemm"] = gmm
         if vl:
             vl["roofline"] = {"bound": "hbm", "achieved": round(vl["value"] / world, 1),
                               "peak": hbm, "unit": "GB/s",
@@ -838,7 +904,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--only", choices=["decode", "e2e", "prefill", "longctx", "varlen",
                                        "kvstate", "qwen35", "decode_step",
-                                       "prefill_chunk"],
+                                       "prefill_chunk", "gemm"],
                     default=None,
                     help="profiling aid: run the decode timing plus only this extra part")
     ap.add_argument("--batch", type=int, default=WL["B"],
