@@ -210,23 +210,35 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
       const bool rv = row < M;
       const uint32_t acc = tl + b * kBN;
       if (Epi == 0) {
-#pragma unroll 1
+        // the residual of chunk c + 1 is in flight while chunk c is added and
+        // stored (one global round trip per tile instead of one per chunk)
+        const float* crow = c_in + static_cast<size_t>(row) * ldc;
+        auto full = [&](int c) { return rv && n0 + c * 32 + 32 <= N; };
+        float4 rc[8], rn[8];
+        if (c_in && full(0)) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) rc[i] = *reinterpret_cast<const float4*>(crow + n0 + 4 * i);
+        }
+#pragma unroll
         for (int c = 0; c < kBN / 32; ++c) {
           float v[32];
           tc_ld32(acc + c * 32, v);
+          if (c + 1 < kBN / 32 && c_in && full(c + 1)) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              rn[i] = *reinterpret_cast<const float4*>(crow + n0 + (c + 1) * 32 + 4 * i);
+          }
           tc_wait_ld();
           const int col = n0 + c * 32;
           if (rv && col < N) {
             if (col + 32 <= N) {
               if (c_in) {
-                const float* cr = c_in + static_cast<size_t>(row) * ldc + col;
 #pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                  const float4 r = *reinterpret_cast<const float4*>(cr + i);
-                  v[i] += r.x;
-                  v[i + 1] += r.y;
-                  v[i + 2] += r.z;
-                  v[i + 3] += r.w;
+                for (int i = 0; i < 8; ++i) {
+                  v[4 * i] += rc[i].x;
+                  v[4 * i + 1] += rc[i].y;
+                  v[4 * i + 2] += rc[i].z;
+                  v[4 * i + 3] += rc[i].w;
                 }
               }
               store32<TO>(out + static_cast<size_t>(row) * ldo + col, v);
@@ -241,6 +253,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
               }
             }
           }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) rc[i] = rn[i];
         }
       } else {
         // SwiGLU: columns [0,128) of the tile are gate rows, [128,256) the up rows
