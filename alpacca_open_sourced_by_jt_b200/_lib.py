@@ -87,6 +87,10 @@ SIGNATURES = [
                                  c_int, c_int, c_int, c_void_p]),
     ("b2a_swiglu_rows", c_int, [c_void_p, c_longlong, c_int, c_void_p, c_longlong, c_int, c_int,
                                 c_int, c_void_p]),
+    ("b2a_q8_gemv_qkv_rope", c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_float,
+                                     c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
+                                     c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+                                     c_void_p]),
     ("b2a_gemm", c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_int, c_void_p, c_longlong,
                          c_void_p, c_longlong, c_int, c_int, c_int, c_int, c_int, c_void_p]),
 ]

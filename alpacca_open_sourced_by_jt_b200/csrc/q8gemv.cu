@@ -49,11 +49,48 @@ __device__ __forceinline__ uint32_t codes_f16x2(uint32_t biased, uint32_t sel) {
   return *reinterpret_cast<const uint32_t*>(&r);
 }
 
-template <int Mode, int Epi, int kWarps>
+// Where the QKV epilogue (Epi 3) puts the rotated q row and the step's K/V
+// cache rows: rows [0, H*D) of the product are q, then KV*D of k, then v.
+struct QkvRope {
+  const float* cos_tab;  // [tab_rows][D/2]
+  const float* sin_tab;
+  const int* pos;        // the token's position (one int, device memory)
+  void* k_cache;         // [n_ctx][KV][D] of the cache type
+  void* v_cache;
+  int tab_rows, n_ctx, H, KV, D;
+};
+
+// RoPE (norm style: pairs 2i, 2i+1 of a head, model.py:1162-1209 with the
+// reference's f32 product order) of one output row whose pair partner is
+// `other`, then the row's store: q into out, k and v into the cache row
+// at the token's position (model.py:1431-1432).
+template <typename TK>
+__device__ __forceinline__ void qkv_rope_store(const QkvRope& rp, int p, int row, float self,
+                                               float other, float* __restrict__ out) {
+  const int qd = rp.H * rp.D, kd = rp.KV * rp.D;
+  if (row < qd + kd) {
+    const int d = row % rp.D, i = d >> 1;
+    const float c = rp.cos_tab[static_cast<size_t>(p) * (rp.D >> 1) + i];
+    const float sn = rp.sin_tab[static_cast<size_t>(p) * (rp.D >> 1) + i];
+    const bool odd = d & 1;
+    const float x0 = odd ? other : self, x1 = odd ? self : other;
+    const float y = odd ? __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c))
+                        : __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+    if (row < qd) {
+      out[row] = y;
+    } else {
+      st_elem(static_cast<TK*>(rp.k_cache) + static_cast<size_t>(p) * kd + (row - qd), y);
+    }
+  } else {
+    st_elem(static_cast<TK*>(rp.v_cache) + static_cast<size_t>(p) * kd + (row - qd - kd), self);
+  }
+}
+
+template <int Mode, int Epi, int kWarps, typename TK = float>
 __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(
     const uint4* __restrict__ tiles, const uint32_t* __restrict__ scales, int rows, int cols,
     int kw, const float* __restrict__ x, const float* __restrict__ aux, float eps,
-    float* __restrict__ out) {
+    float* __restrict__ out, const QkvRope rp) {
   constexpr int kThreads = kWarps * 32;
   extern __shared__ uint4 xs[];  // [nb][8]: B fragments (hi for lanes 0-3, lo for 4-7)
   __shared__ double red[kWarps];
@@ -213,7 +250,22 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(
         }
       }
     }
-    if (ks == 0 && tp == 0 && rg < rgs) {
+    if (Epi == 3) {
+      if (ks == 0) {  // the pair partner of row 16rg + g is row 16rg + (g ^ 1): lane ^ 4
+        const float pa = __shfl_xor_sync(0xffffffffu, acc_a, 4);
+        const float pb = __shfl_xor_sync(0xffffffffu, acc_b, 4);
+        if (tp == 0 && rg < rgs) {
+          const int p = *rp.pos;
+          if (p < 0 || p >= rp.n_ctx || p >= rp.tab_rows) {
+            if (g == 0) set_dev_error(B2A_ERR_POSITION, p);
+          } else {
+            const int ra = rg * 16 + g;
+            if (ra < rows) qkv_rope_store<TK>(rp, p, ra, acc_a, pa, out);
+            if (ra + 8 < rows) qkv_rope_store<TK>(rp, p, ra + 8, acc_b, pb, out);
+          }
+        }
+      }
+    } else if (ks == 0 && tp == 0 && rg < rgs) {
       const int ra = rg * 16 + g, rb = ra + 8;
       if (Epi == 2) {
         const int i = rg * 8 + g;  // gate row ra, up row rb
@@ -251,10 +303,11 @@ __global__ void embed_kernel(const int8_t* __restrict__ codes, const __half* __r
 
 namespace {
 
-template <int Mode, int Epi, int W>
+template <int Mode, int Epi, int W, typename TK = float>
 int launch_gemv_w(const int8_t* codes, const __half* scales, int rows, int cols, const float* x,
-                  const float* aux, float eps, float* out, bool pdl, cudaStream_t st) {
-  auto kern = b2a::q8::gemv_kernel<Mode, Epi, W>;
+                  const float* aux, float eps, float* out, bool pdl, cudaStream_t st,
+                  const b2a::q8::QkvRope& rp = b2a::q8::QkvRope{}) {
+  auto kern = b2a::q8::gemv_kernel<Mode, Epi, W, TK>;
   const int smem = cols * 4;  // 8 uint4 B fragments per 32-column block
   if (smem > 48 * 1024) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -287,7 +340,7 @@ int launch_gemv_w(const int8_t* codes, const __half* scales, int rows, int cols,
   cfg.numAttrs = pdl ? 1 : 0;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, reinterpret_cast<const uint4*>(codes),
                                            reinterpret_cast<const uint32_t*>(scales), rows, cols,
-                                           kw, x, aux, eps, out);
+                                           kw, x, aux, eps, out, rp);
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "q8_gemv launch");
   return B2A_OK;
 }
@@ -343,6 +396,44 @@ int b2a_q8_gemv(const void* codes, const void* scales, int rows, int cols, const
     default: B2A_GEMV_CASE(2);
   }
 #undef B2A_GEMV_CASE
+}
+
+int b2a_q8_gemv_qkv_rope(const void* codes, const void* scales, int cols, const float* x,
+                         const float* norm_w, float eps, float* q_out, const float* cos_tab,
+                         const float* sin_tab, int tab_rows, const int* pos_dev, void* k_cache,
+                         void* v_cache, int kv_dtype, int n_ctx, int H, int KV, int D, int flags,
+                         void* stream) {
+  using b2a_host::fail;
+  if (!codes || !scales || !x || !norm_w || !q_out || !cos_tab || !sin_tab || !pos_dev ||
+      !k_cache || !v_cache)
+    return fail(B2A_ERR_ARG, "q8_gemv_qkv_rope: null pointer argument");
+  if (H <= 0 || KV <= 0 || D <= 0 || (D & 1) || n_ctx <= 0 || tab_rows <= 0)
+    return fail(B2A_ERR_SHAPE, "q8_gemv_qkv_rope: H=%d KV=%d D=%d (even) n_ctx=%d", H, KV, D,
+                n_ctx);
+  if (cols <= 0 || (cols & 31)) return fail(B2A_ERR_SHAPE, "q8_gemv_qkv_rope: cols %d", cols);
+  if (cols > 16384) return fail(B2A_ERR_UNSUPPORTED, "q8_gemv_qkv_rope: cols %d > 16384", cols);
+  if (!b2a_host::aligned16(codes) || (reinterpret_cast<uintptr_t>(scales) & 3) ||
+      !b2a_host::aligned16(x) || !b2a_host::aligned16(norm_w))
+    return fail(B2A_ERR_ALIGN, "q8_gemv_qkv_rope: tiles, x and norm_w 16-byte aligned, scales 4-byte");
+  if (!(eps > 0.f)) return fail(B2A_ERR_ARG, "q8_gemv_qkv_rope: eps must be > 0");
+  if (flags & ~B2A_GEMV_PDL) return fail(B2A_ERR_ARG, "q8_gemv_qkv_rope: flags %#x", flags);
+  const int rows = (H + 2 * KV) * D;
+  const b2a::q8::QkvRope rp{cos_tab, sin_tab, pos_dev, k_cache, v_cache, tab_rows, n_ctx, H, KV, D};
+  const int8_t* c = static_cast<const int8_t*>(codes);
+  const __half* sc = static_cast<const __half*>(scales);
+  const bool pdl = flags & B2A_GEMV_PDL;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool wide = cols / 32 >= 256 && (rows + 15) / 16 <= 512;
+#define B2A_QKV_CASE(TK)                                                                    \
+  return wide ? launch_gemv_w<1, 3, 16, TK>(c, sc, rows, cols, x, norm_w, eps, q_out, pdl, st, rp) \
+              : launch_gemv_w<1, 3, 8, TK>(c, sc, rows, cols, x, norm_w, eps, q_out, pdl, st, rp)
+  switch (kv_dtype) {
+    case B2A_F32: B2A_QKV_CASE(float);
+    case B2A_F16: B2A_QKV_CASE(__half);
+    case B2A_BF16: B2A_QKV_CASE(__nv_bfloat16);
+  }
+#undef B2A_QKV_CASE
+  return fail(B2A_ERR_DTYPE, "q8_gemv_qkv_rope: kv_dtype %d", kv_dtype);
 }
 
 int b2a_q8_embed(const void* codes, const void* scales, int rows, int cols,

@@ -4,12 +4,13 @@ The reference's GPU decode chain (alpaccaroo/cuda.py:1682-2159,
 DecodeChain.step at :2082-2159) runs a token as a sequence of Numba-CUDA
 launches over Q8_0 weights in VRAM; Model._forward_np (model.py:1374-1487)
 is the same computation on the host.  Here a token is one CUDA graph of
-6 launches per layer plus 3:
+5 launches per layer plus 3:
 
   embed       one dequantized Q8_0 embedding row          (b2a_q8_embed)
   per layer:
-    qkv     = Wqkv . RMSNorm(x)          (fused RMSNorm; Wq|Wk|Wv rows)  b2a_q8_gemv
-    RoPE of q and k, k/v stored at the position            b2a_rope_append
+    qkv     = Wqkv . RMSNorm(x)          (fused RMSNorm; Wq|Wk|Wv rows), with
+              RoPE of q and k and the k/v rows stored at the position in
+              the epilogue                                 b2a_q8_gemv_qkv_rope
     att     = GQA decode over positions 0..pos             b2a_decode (2 kernels)
     x      += Wo . att                   (residual in the epilogue)      b2a_q8_gemv
     act     = SwiGLU(Wgu . RMSNorm(x))   (gate/up rows interleaved, the
@@ -21,8 +22,8 @@ is the same computation on the host.  Here a token is one CUDA graph of
 with the token id and position copied from pinned host memory at the start
 of the graph and the logits copied back at its end.  The matrix-vector
 products are programmatic dependents of the kernel before them: each
-prefetches its weights into L2 while that kernel finishes (the weights do
-not depend on the activations).
+starts loading its weights while that kernel finishes (the weights do not
+depend on the activations).
 """
 from __future__ import annotations
 
@@ -146,6 +147,25 @@ class Q8Matrix:
         return out
 
 
+    def gemv_qkv_rope(self, x: torch.Tensor, norm_w: torch.Tensor, eps: float, q_out, cos_tab,
+                      sin_tab, pos: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                      H: int, KV: int, D: int, *, flags: int = 0, stream=None):
+        """This matrix as a layer's [q; k; v] projection of RMSNorm(x), with
+        RoPE (norm style) and the K/V append at position *pos fused into its
+        epilogue (b2a_q8_gemv_qkv_rope): rotated q into q_out, k and v into
+        the caches' row pos."""
+        if self.rows != (H + 2 * KV) * D:
+            raise _lib.B2AShapeError(_lib.ERR_SHAPE, f"{self.rows} rows for H={H} KV={KV} D={D}")
+        tiles, ts = self.tiles()
+        _lib.check(_lib.load().b2a_q8_gemv_qkv_rope(
+            tiles.data_ptr(), ts.data_ptr(), self.cols, x.data_ptr(), norm_w.data_ptr(),
+            float(eps), q_out.data_ptr(), cos_tab.data_ptr(), sin_tab.data_ptr(),
+            cos_tab.shape[0], pos.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+            device._code(k_cache.dtype), k_cache.shape[-3], H, KV, D, int(flags),
+            device._stream(stream)))
+        return q_out
+
+
 class LlamaQ8:
     """Weights of a llama-architecture model with Q8_0 matrices, on the device."""
 
@@ -249,7 +269,7 @@ class DecodeChain:
         self._graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self._graph, stream=self._stream):
             self._body()
-        self.launches = 3 + 6 * len(m.layers)
+        self.launches = 3 + 5 * len(m.layers)
 
     def _body(self):
         m = self.m
@@ -264,16 +284,12 @@ class DecodeChain:
         v = self.qkv[qd + kd:].view(1, m.KV, m.D)
         pos, lens = self._d_i[1:2], self._d_i[2:3]
         for li, ly in enumerate(m.layers):
-            ly["wqkv"].gemv(self.x, self.qkv, mode=1, aux=ly["attn_norm"], eps=m.eps,
-                            flags=PDL)
-            # RoPE + append starts while the QKV GEMV drains (programmatic
-            # launch; its position comes from the host copy at the head of
-            # the graph).  The decode and the GEMVs after it measured no
-            # better launched that way: their early starts take bandwidth
-            # from the kernel on the critical path.
-            with device.launch_flags(_lib.LAUNCH_PDL):
-                device.rope_append(q, k, v, pos, self.cos, self.sin, k_cache=self.k_cache[li],
-                                   v_cache=self.v_cache[li])
+            # QKV with the attention norm in front and RoPE + the K/V append
+            # in its epilogue (the position comes from the host copy at the
+            # head of the graph)
+            ly["wqkv"].gemv_qkv_rope(self.x, ly["attn_norm"], m.eps, self.qkv, self.cos,
+                                     self.sin, pos, self.k_cache[li], self.v_cache[li], m.H,
+                                     m.KV, m.D, flags=PDL)
             device.decode(q, self.k_cache[li], self.v_cache[li], lens, max_len=self.n_ctx,
                           out=self.att, workspace=self._ws, split_rows=self._split)
             ly["wo"].gemv(self.att, self.x, flags=ACCUMULATE | PDL)

@@ -293,6 +293,24 @@ int b2a_sigmoid_gate(const float* values, long long value_row_stride, const floa
 int b2a_q8_gemv(const void* codes, const void* scales, int rows, int cols, const float* x,
                 const float* aux, int mode, float eps, float* out, int flags, void* stream);
 
+/* A decode step's QKV projection with the RMSNorm in front and RoPE + K/V
+ * append in the epilogue: the Q8_0 GEMV of b2a_q8_gemv (mode 1, the
+ * attention norm weight norm_w) over the (H + 2*KV)*D rows [q; k; v] of
+ * a llama layer, then, at the position *pos_dev (the token's cache row):
+ *   q rows  rotated (norm style: pairs 2i, 2i+1 of each head, the
+ *           reference's f32 products, model.py:1162-1209) into q_out
+ *           (f32 [H*D])
+ *   k rows  rotated into k_cache row pos ([n_ctx][KV][D] of kv_dtype)
+ *   v rows  into v_cache row pos (model.py:1431-1432)
+ * cos_tab / sin_tab f32 [tab_rows][D/2] (model.py:318-323).  flags: 0 or
+ * B2A_GEMV_PDL.  A position outside the cache or table records
+ * B2A_ERR_POSITION.  One launch instead of the GEMV plus b2a_rope_append. */
+int b2a_q8_gemv_qkv_rope(const void* codes, const void* scales, int cols, const float* x,
+                         const float* norm_w, float eps, float* q_out, const float* cos_tab,
+                         const float* sin_tab, int tab_rows, const int* pos_dev, void* k_cache,
+                         void* v_cache, int kv_dtype, int n_ctx, int H, int KV, int D, int flags,
+                         void* stream);
+
 /* out[i][c] = q[tok_i][c] * d[tok_i][c/32] for the n_tok tokens read from
  * tokens_dev: dequantized Q8_0 embedding rows (qmatrix.py:445-447;
  * T.matrix_row / matrix_rows at model.py:1396, :1308).  A token outside

@@ -99,4 +99,34 @@ def test_chain_matches_reference_logits(cuda_dev, golden, kv_dtype, tol):
     for pos, tok in enumerate(c["tokens"]):
         logits = chain(tok, pos).numpy()
         assert rel_err(logits, g["logits"][pos]) < tol, pos
-    assert chain.launches == 3 + 6 * c["n_layer"]
+    assert chain.launches == 3 + 5 * c["n_layer"]
+
+
+@pytest.mark.parametrize("kv_dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("H,KV,D,cols", [(32, 8, 64, 2048), (2, 1, 64, 8192), (4, 2, 128, 256)])
+def test_qkv_rope_epilogue_matches_two_launches(cuda_dev, kv_dtype, H, KV, D, cols):
+    """b2a_q8_gemv_qkv_rope against the GEMV (RMSNorm mode) followed by
+    b2a_rope_append: the same products, rotation and stores, so q and the
+    cache rows must agree bit for bit; the other cache rows stay untouched."""
+    from alpacca_open_sourced_by_jt_b200 import device
+    from alpacca_open_sourced_by_jt_b200.decode_chain import Q8Matrix
+    rng = np.random.default_rng(H * D + cols)
+    rows, n_ctx = (H + 2 * KV) * D, 64
+    w = Q8Matrix.from_q8_0(_q8(rng, rows, cols), rows, cols, cuda_dev)
+    x = torch.from_numpy(rng.standard_normal(cols).astype(np.float32)).to(cuda_dev)
+    nw = torch.from_numpy((1.0 + 0.1 * rng.standard_normal(cols)).astype(np.float32)).to(cuda_dev)
+    ct, st = device.rope_tables(n_ctx, D, 500000.0, device=cuda_dev)
+    pos = torch.tensor([37], dtype=torch.int32, device=cuda_dev)
+    base = torch.from_numpy(rng.standard_normal((1, n_ctx, KV, D)).astype(np.float32)).to(
+        cuda_dev).to(kv_dtype)
+    k_ref, v_ref, k_got, v_got = base.clone(), base.clone(), base.clone(), base.clone()
+    qkv = torch.zeros(rows, dtype=torch.float32, device=cuda_dev)
+    w.gemv(x, qkv, mode=1, aux=nw, eps=1e-5)
+    qd, kd = H * D, KV * D
+    device.rope_append(qkv[:qd].view(1, H, D), qkv[qd:qd + kd].view(1, KV, D),
+                       qkv[qd + kd:].view(1, KV, D), pos, ct, st, k_cache=k_ref, v_cache=v_ref)
+    q_got = torch.zeros(rows, dtype=torch.float32, device=cuda_dev)
+    w.gemv_qkv_rope(x, nw, 1e-5, q_got, ct, st, pos, k_got, v_got, H, KV, D, flags=4)
+    torch.cuda.synchronize()
+    assert torch.equal(q_got[:qd], qkv[:qd])
+    assert torch.equal(k_got, k_ref) and torch.equal(v_got, v_ref)
