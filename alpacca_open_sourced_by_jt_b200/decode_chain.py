@@ -4,14 +4,14 @@ The reference's GPU decode chain (alpaccaroo/cuda.py:1682-2159,
 DecodeChain.step at :2082-2159) runs a token as a sequence of Numba-CUDA
 launches over Q8_0 weights in VRAM; Model._forward_np (model.py:1374-1487)
 is the same computation on the host.  Here a token is one CUDA graph of
-5 launches per layer plus 3:
+98 kernel launches: the embedding gather, 6 per layer, the LM head:
 
   embed       one dequantized Q8_0 embedding row          (b2a_q8_embed)
   per layer:
     qkv     = Wqkv . RMSNorm(x)          (fused RMSNorm; Wq|Wk|Wv rows), with
               RoPE of q and k and the k/v rows stored at the position in
               the epilogue                                 b2a_q8_gemv_qkv_rope
-    att     = GQA decode over positions 0..pos             b2a_decode (2 kernels)
+    att     = GQA decode over positions 0..pos             b2a_decode (split + combine)
     x      += Wo . att                   (residual in the epilogue)      b2a_q8_gemv
     act     = SwiGLU(Wgu . RMSNorm(x))   (gate/up rows interleaved, the
                                           SwiGLU of each row pair in the
@@ -269,7 +269,7 @@ class DecodeChain:
         self._graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self._graph, stream=self._stream):
             self._body()
-        self.launches = 3 + 5 * len(m.layers)
+        self.launches = 2 + 6 * len(m.layers)  # kernels per token
 
     def _body(self):
         m = self.m

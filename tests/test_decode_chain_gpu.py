@@ -99,7 +99,7 @@ def test_chain_matches_reference_logits(cuda_dev, golden, kv_dtype, tol):
     for pos, tok in enumerate(c["tokens"]):
         logits = chain(tok, pos).numpy()
         assert rel_err(logits, g["logits"][pos]) < tol, pos
-    assert chain.launches == 3 + 5 * c["n_layer"]
+    assert chain.launches == 2 + 6 * c["n_layer"]
 
 
 @pytest.mark.parametrize("kv_dtype", [torch.float32, torch.float16, torch.bfloat16])
