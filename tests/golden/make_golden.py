@@ -1,9 +1,9 @@
 """Generate golden vectors by running the REFERENCE (alpaccaroo) itself.
 
-Run in a container that has the reference checked out (default path below,
-or ALPACCAROO_REF=<dir containing the alpaccaroo package>):
+Run where the reference is checked out, naming the directory that holds the
+alpaccaroo package:
 
-    python tests/golden/make_golden.py
+    ALPACCAROO_REF=<checkout> python tests/golden/make_golden.py
 
 Inputs are regenerated from their seeds by tests/golden/cases.py (NumPy's
 PCG64 default_rng is stable across versions); each .npz stores the
@@ -24,10 +24,13 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
 from tests.golden import cases  # noqa: E402
 
-REF = os.environ.get("ALPACCAROO_REF", "/root/reference")
+REF = os.environ.get("ALPACCAROO_REF")  # the alpaccaroo source checkout
 
 
 def _import_reference():
+    if not REF:
+        sys.exit("set ALPACCAROO_REF to the alpaccaroo source checkout (the directory "
+                 "holding the alpaccaroo package)")
     sys.path.insert(0, REF)
     from alpaccaroo import model, qwen35_kernels, qwen35_ops  # noqa: WPS433
     return model, qwen35_kernels, qwen35_ops
