@@ -491,10 +491,41 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(
   }
   __syncthreads();
   const float invL = s_invL;
-  for (int d = threadIdx.x; d < D; d += kCombineThreads) {
-    float acc = 0.f;
-    for (int s = 0; s < ns; ++s) acc += part_o[(p0 + s) * D + d] * wsm[s];
-    out[static_cast<size_t>(bh) * D + d] = acc * invL;
+  if (D <= kCombineThreads) {
+    // every thread works: thread t sums splits t / D, t / D + nh, ... of
+    // output column t % D (four loads in flight), then the nh partial sums
+    // of each column meet in shared memory in a fixed order
+    const int nh = kCombineThreads / D, h = threadIdx.x / D, d = threadIdx.x - h * D;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    if (h < nh) {
+      int s = h;
+      for (; s + 3 * nh < ns; s += 4 * nh) {
+        a0 += part_o[(p0 + s) * D + d] * wsm[s];
+        a1 += part_o[(p0 + s + nh) * D + d] * wsm[s + nh];
+        a2 += part_o[(p0 + s + 2 * nh) * D + d] * wsm[s + 2 * nh];
+        a3 += part_o[(p0 + s + 3 * nh) * D + d] * wsm[s + 3 * nh];
+      }
+      for (; s < ns; s += nh) a0 += part_o[(p0 + s) * D + d] * wsm[s];
+    }
+    __shared__ float part[kCombineThreads];
+    part[threadIdx.x] = (a0 + a1) + (a2 + a3);
+    __syncthreads();
+    if (static_cast<int>(threadIdx.x) < D) {
+      float acc = 0.f;
+      for (int j = 0; j < nh; ++j) acc += part[j * D + threadIdx.x];
+      out[static_cast<size_t>(bh) * D + threadIdx.x] = acc * invL;
+    }
+  } else {
+    for (int d = threadIdx.x; d < D; d += kCombineThreads) {
+      float a0 = 0.f, a1 = 0.f;
+      int s = 0;
+      for (; s + 1 < ns; s += 2) {
+        a0 += part_o[(p0 + s) * D + d] * wsm[s];
+        a1 += part_o[(p0 + s + 1) * D + d] * wsm[s + 1];
+      }
+      if (s < ns) a0 += part_o[(p0 + s) * D + d] * wsm[s];
+      out[static_cast<size_t>(bh) * D + d] = (a0 + a1) * invL;
+    }
   }
 }
 
