@@ -290,8 +290,13 @@ class DecodeChain:
             ly["wqkv"].gemv_qkv_rope(self.x, ly["attn_norm"], m.eps, self.qkv, self.cos,
                                      self.sin, pos, self.k_cache[li], self.v_cache[li], m.H,
                                      m.KV, m.D, flags=PDL)
-            device.decode(q, self.k_cache[li], self.v_cache[li], lens, max_len=self.n_ctx,
-                          out=self.att, workspace=self._ws, split_rows=self._split)
+            # the decode (and its combine) as programmatic dependents: the
+            # split CTAs stream the cache rows below the newest while the QKV
+            # GEMV, latency-bound, still runs; they read q and the new row
+            # after it completes (the length comes from the host copy above)
+            with device.launch_flags(_lib.LAUNCH_PDL):
+                device.decode(q, self.k_cache[li], self.v_cache[li], lens, max_len=self.n_ctx,
+                              out=self.att, workspace=self._ws, split_rows=self._split)
             ly["wo"].gemv(self.att, self.x, flags=ACCUMULATE | PDL)
             ly["wgu"].gemv(self.x, self.act, mode=1, aux=ly["ffn_norm"], eps=m.eps,
                            flags=SWIGLU_OUT | PDL)
