@@ -16,7 +16,12 @@ any size (the oracle's NumPy einsum would take minutes there):
   statement of the multi-GPU split;
 * config 3 (64 sequences, lengths uniform in [1024, 8192] from seed 2, fp16
   cache): every sequence of the batch equals that sequence decoded alone
-  with the same split size, bit for bit (no cross-sequence state).
+  with the same split size, bit for bit (no cross-sequence state);
+* config 2 (causal prefill, 2048 tokens, 32 q / 8 KV heads, head_dim 128,
+  bf16): the chunk in two halves (the second over the whole key range,
+  split on a 128-row query tile) equals the single call bit for bit, for the
+  paired-head and the one-head kernels, since every query tile visits the
+  same key tiles in the same order either way.
 """
 import numpy as np
 import pytest
@@ -101,3 +106,25 @@ def test_config3_batch_equals_each_sequence_alone(cuda_dev):
         one = device.decode(q[b:b + 1].contiguous(), k[b:b + 1], v[b:b + 1], lens[b:b + 1],
                             split_rows=split, max_len=Lmax)
         assert torch.equal(one[0], batch[b]), b
+
+
+@pytest.mark.parametrize("kernel", ["pair", "head"])
+def test_config2_prefill_in_two_chunks_is_bit_identical(cuda_dev, monkeypatch, kernel):
+    from alpacca_open_sourced_by_jt_b200 import device
+    if kernel == "head":
+        monkeypatch.setenv("B2ATTN_PREFILL", "head")
+    else:
+        monkeypatch.delenv("B2ATTN_PREFILL", raising=False)
+    S, H, KV, D = 2048, 32, 8, 128
+    g = torch.Generator(device=cuda_dev).manual_seed(1)
+    q = _rand((S, H, D), torch.bfloat16, cuda_dev, g)
+    k = _rand((S, KV, D), torch.bfloat16, cuda_dev, g)
+    v = _rand((S, KV, D), torch.bfloat16, cuda_dev, g)
+    pos = torch.arange(S, dtype=torch.int32, device=cuda_dev)
+    full = device.prefill(q, k, v, pos)
+    h = S // 2
+    first = device.prefill(q[:h].contiguous(), k[:h].contiguous(), v[:h].contiguous(), pos[:h].contiguous())
+    second = device.prefill(q[h:].contiguous(), k, v, pos[h:].contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(torch.cat([first, second]), full)
+
