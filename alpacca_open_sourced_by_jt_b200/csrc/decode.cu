@@ -41,7 +41,7 @@ struct Cfg {
   static constexpr int kBoxBytes = kRows * 128;    // one box = 64 rows x 128 B
   static constexpr int kTileBytes = kBoxes * kBoxBytes;
   static constexpr int kStageBytes = 2 * kTileBytes;  // K tile + V tile
-  static constexpr int kStages = D == 64 ? 4 : (D == 128 ? 3 : 2);
+  static constexpr int kStages = D == 64 ? 4 : 3;
   static constexpr int kRingBytes = kStages * kStageBytes;
 };
 
