@@ -69,8 +69,8 @@ const char* b2a_last_error(void);
 int b2a_device_error(int* code, int* aux, int clear);
 
 /* Launch mode of the calling thread's later launches; returns the previous
- * flags.  B2A_LAUNCH_PDL launches b2a_rope_append, b2a_qwen35_attn_prep's
- * IMROPE append, b2a_decode (both kernels) and b2a_lse_combine as
+ * flags.  B2A_LAUNCH_PDL launches b2a_rope_append, b2a_imrope_append,
+ * b2a_decode (both kernels), b2a_lse_combine and b2a_gemm as
  * programmatic dependents of the kernel before them on the stream: each
  * starts while that kernel drains and waits for it (griddepcontrol.wait)
  * before reading what it wrote.  The decode's K/V rows below the newest
