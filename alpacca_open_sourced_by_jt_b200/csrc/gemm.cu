@@ -14,6 +14,10 @@
 // (gate rows 128g..128g+127, then the matching up rows) and writes the
 // activation the down projection reads (model.py:1352-1354).
 //
+// QKV_ROPE (b2a_gemm_qkv_rope) takes w = [Wq; Wk; Wv] and writes q rotated
+// (16-bit) plus the rotated k and the v rows at each token's cache position,
+// the work of b2a_rope_append, from the fp32 accumulator.
+//
 // Kernel: persistent, one CTA per SM, 128 x 256 output tiles taken in
 // m-fastest order (the CTAs working at one time share a weight tile, which
 // then comes from L2).  256 threads:
@@ -85,11 +89,24 @@ __device__ __forceinline__ void store32<__half>(__half* dst, const float* v) {
   }
 }
 
+// Where the QKV epilogue (Epi 2) puts a prefill chunk's rows: columns
+// [0, H*D) of the product are q, then KV*D of k, then v; row m is the token
+// at position pos[m].
+struct QkvRope {
+  const int* pos;        // [M] cache row of each token
+  const float* cos_tab;  // [tab_rows][D/2]
+  const float* sin_tab;
+  void* q_out;           // [M][H*D] rotated q, 16-bit
+  void* k_cache;         // [n_ctx][KV][D], 16-bit
+  void* v_cache;
+  int tab_rows, n_ctx, H, KV, D;
+};
+
 template <typename T, typename TO, int Epi>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
     const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
     const float* __restrict__ c_in, long long ldc, TO* __restrict__ out, long long ldo, int M,
-    int N, int K) {
+    int N, int K, const QkvRope rp) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_full[kStages], bar_empty[kStages];
   __shared__ __align__(8) uint64_t bar_acc_full[2], bar_acc_empty[2];
@@ -256,6 +273,61 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
 #pragma unroll
           for (int i = 0; i < 8; ++i) rc[i] = rn[i];
         }
+      } else if (Epi == 2) {
+        // RoPE (norm style, pairs 2i, 2i+1 of a head: adjacent columns of this
+        // thread's row, the reference's f32 products, model.py:1162-1209),
+        // then q into q_out and k, v into the cache row at the token's
+        // position (model.py:1335-1337); D % 32 == 0, so a 32-column chunk
+        // lies inside one head
+        const int qd = rp.H * rp.D, kd = rp.KV * rp.D, half = rp.D >> 1;
+        int p = -1;
+        if (rv) {
+          p = rp.pos[row];
+          if (p < 0 || p >= rp.n_ctx || p >= rp.tab_rows) {
+            set_dev_error(B2A_ERR_POSITION, row);
+            p = -1;
+          }
+        }
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          const int col = n0 + c * 32;
+          if (col >= N) break;
+          float v[32];
+          tc_ld32(acc + c * 32, v);
+          // this row's 16 cos and 16 sin entries (64 aligned bytes each),
+          // fetched while the accumulator chunk comes out of TMEM
+          const bool rot = p >= 0 && col < qd + kd;
+          float4 cs4[4], sn4[4];
+          if (rot) {
+            const size_t at = static_cast<size_t>(p) * half + ((col % rp.D) >> 1);
+            const float4* ct = reinterpret_cast<const float4*>(rp.cos_tab + at);
+            const float4* st = reinterpret_cast<const float4*>(rp.sin_tab + at);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              cs4[i] = ct[i];
+              sn4[i] = st[i];
+            }
+          }
+          tc_wait_ld();
+          if (p >= 0) {
+            if (rot) {
+              const float* cs = reinterpret_cast<const float*>(cs4);
+              const float* sn = reinterpret_cast<const float*>(sn4);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const float x0 = v[2 * i], x1 = v[2 * i + 1];
+                v[2 * i] = __fsub_rn(__fmul_rn(x0, cs[i]), __fmul_rn(x1, sn[i]));
+                v[2 * i + 1] = __fadd_rn(__fmul_rn(x0, sn[i]), __fmul_rn(x1, cs[i]));
+              }
+            }
+            TO* dst = col < qd ? static_cast<TO*>(rp.q_out) + static_cast<size_t>(row) * qd + col
+                      : col < qd + kd
+                          ? static_cast<TO*>(rp.k_cache) + static_cast<size_t>(p) * kd + (col - qd)
+                          : static_cast<TO*>(rp.v_cache) + static_cast<size_t>(p) * kd +
+                                (col - qd - kd);
+            store32<TO>(dst, v);
+          }
+        }
       } else {
         // SwiGLU: columns [0,128) of the tile are gate rows, [128,256) the up rows
 #pragma unroll 1
@@ -295,7 +367,8 @@ namespace {
 
 template <typename T, typename TO, int Epi>
 int launch_gemm(const void* a, long long lda, const void* w, long long ldw, const float* c_in,
-                long long ldc, void* out, long long ldo, int M, int N, int K, cudaStream_t st) {
+                long long ldc, void* out, long long ldo, int M, int N, int K, cudaStream_t st,
+                const b2a::gemm::QkvRope& rp = b2a::gemm::QkvRope{}) {
   namespace G = b2a::gemm;
   auto kern = G::gemm_kernel<T, TO, Epi>;
   const CUtensorMapDataType tdt = std::is_same<T, __nv_bfloat16>::value
@@ -314,15 +387,16 @@ int launch_gemm(const void* a, long long lda, const void* w, long long ldw, cons
   rc = b2a_host::make_tmap(&tw, tdt, 2, const_cast<void*>(w), wdims, wstr, wbox,
                            CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
+  constexpr int smem_bytes = G::kSmem;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "cudaFuncSetAttribute(gemm)");
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int tiles = ((M + G::kBM - 1) / G::kBM) * ((N + G::kBN - 1) / G::kBN);
   const int grid = tiles < sms ? tiles : sms;
-  e = b2a_host::launch(kern, dim3(grid), dim3(G::kThreads), G::kSmem, st, ta, tw, c_in, ldc,
-                       static_cast<TO*>(out), ldo, M, N, K);
+  e = b2a_host::launch(kern, dim3(grid), dim3(G::kThreads), smem_bytes, st, ta, tw, c_in, ldc,
+                       static_cast<TO*>(out), ldo, M, N, K, rp);
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "gemm launch");
   return B2A_OK;
 }
@@ -378,6 +452,36 @@ int b2a_gemm(const void* a, long long lda, const void* w, long long ldw, int dty
                ? gemm_out<__half, 1>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st)
                : gemm_out<__half, 0>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
   return fail(B2A_ERR_DTYPE, "gemm: operand dtype %d (f16 or bf16)", dtype);
+}
+
+int b2a_gemm_qkv_rope(const void* a, long long lda, const void* w, long long ldw, int dtype,
+                      int M, int K, const int* pos_dev, const float* cos_tab, const float* sin_tab,
+                      int tab_rows, int H, int KV, int D, void* q_out, void* k_cache,
+                      void* v_cache, int n_ctx, void* stream) {
+  using b2a_host::fail;
+  if (!a || !w || !pos_dev || !cos_tab || !sin_tab || !q_out || !k_cache || !v_cache)
+    return fail(B2A_ERR_ARG, "gemm_qkv_rope: null pointer argument");
+  if (M <= 0 || K <= 0 || H <= 0 || KV <= 0 || n_ctx <= 0 || tab_rows <= 0)
+    return fail(B2A_ERR_SHAPE, "gemm_qkv_rope: M=%d K=%d H=%d KV=%d", M, K, H, KV);
+  if (D <= 0 || D % 32)
+    return fail(B2A_ERR_UNSUPPORTED, "gemm_qkv_rope: head_dim %d (a multiple of 32)", D);
+  if (lda < K || ldw < K || (lda & 7) || (ldw & 7))
+    return fail(B2A_ERR_ALIGN, "gemm_qkv_rope: lda/ldw must be >= K and multiples of 8");
+  if (!b2a_host::aligned16(a) || !b2a_host::aligned16(w) || !b2a_host::aligned16(q_out) ||
+      !b2a_host::aligned16(k_cache) || !b2a_host::aligned16(v_cache) ||
+      !b2a_host::aligned16(cos_tab) || !b2a_host::aligned16(sin_tab))
+    return fail(B2A_ERR_ALIGN,
+                "gemm_qkv_rope: a, w, q_out, the caches and the tables must be 16-byte aligned");
+  const int N = (H + 2 * KV) * D;
+  const b2a::gemm::QkvRope rp{pos_dev, cos_tab, sin_tab, q_out, k_cache, v_cache,
+                              tab_rows, n_ctx, H, KV, D};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == B2A_BF16)
+    return launch_gemm<__nv_bfloat16, __nv_bfloat16, 2>(a, lda, w, ldw, nullptr, 0, nullptr, 0, M,
+                                                        N, K, st, rp);
+  if (dtype == B2A_F16)
+    return launch_gemm<__half, __half, 2>(a, lda, w, ldw, nullptr, 0, nullptr, 0, M, N, K, st, rp);
+  return fail(B2A_ERR_DTYPE, "gemm_qkv_rope: dtype %d (f16 or bf16)", dtype);
 }
 
 }  // extern "C"

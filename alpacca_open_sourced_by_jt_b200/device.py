@@ -308,3 +308,40 @@ def gemm(a: torch.Tensor, w: torch.Tensor, *, out=None, out_dtype=torch.float32,
         0 if c_in is None else c_in.stride(0), _ptr(out), out.stride(0), _code(out.dtype), M, N,
         K, int(epilogue), _stream(stream)))
     return out
+
+
+def gemm_qkv_rope(a: torch.Tensor, w: torch.Tensor, positions: torch.Tensor,
+                  cos_tab: torch.Tensor, sin_tab: torch.Tensor, *, H: int, KV: int, k_cache,
+                  v_cache, q_out, stream=None) -> torch.Tensor:
+    """A chunk's QKV projection with RoPE and the K/V append in the GEMM
+    epilogue (b2a_gemm_qkv_rope): q = (a . w^T)[:, :H*D] rotated into q_out
+    (M, H, D); k rotated and v into the caches' rows `positions`.
+
+    a (M, K) and w ((H + 2*KV)*D, K) 16-bit, unit stride along K; caches
+    (n_ctx, KV, D) or (1, n_ctx, KV, D) of a's dtype; cos/sin f32 (rows,
+    D/2): norm-style RoPE over the whole head.  The same result as gemm()
+    to f32 followed by rope_append(q_out=...)."""
+    _need(a.dim() == 2 and w.dim() == 2 and a.shape[1] == w.shape[1], "a (M,K), w (N,K)")
+    _need(a.dtype == w.dtype and a.dtype in (torch.float16, torch.bfloat16), "16-bit a and w")
+    _need(a.stride(1) == 1 and w.stride(1) == 1, "a and w need unit stride along K")
+    M, K = a.shape
+    if k_cache.dim() == 4:
+        _need(k_cache.shape[0] == 1 and v_cache.shape[0] == 1, "one sequence's cache")
+        k_cache, v_cache = k_cache[0], v_cache[0]
+    _need(k_cache.shape == v_cache.shape and k_cache.dim() == 3, "caches (n_ctx, KV, D)")
+    n_ctx, kv_, D = k_cache.shape
+    _need(kv_ == KV and w.shape[0] == (H + 2 * KV) * D, "w rows must be (H + 2*KV) * D")
+    _need(k_cache.dtype == a.dtype and v_cache.dtype == a.dtype and q_out.dtype == a.dtype,
+          "caches and q_out in a's dtype")
+    for n_, t_ in (("k_cache", k_cache), ("v_cache", v_cache), ("q_out", q_out),
+                   ("positions", positions), ("cos_tab", cos_tab), ("sin_tab", sin_tab)):
+        _cuda_contig(n_, t_)
+    _need(q_out.numel() == M * H * D, "q_out (M, H, D)")
+    _need(positions.dtype == torch.int32 and positions.numel() == M, "positions int32 (M,)")
+    _need(cos_tab.shape == sin_tab.shape and cos_tab.shape[1] * 2 == D,
+          "cos/sin tables (rows, D/2)")
+    _lib.check(_lib.load().b2a_gemm_qkv_rope(
+        _ptr(a), a.stride(0), _ptr(w), w.stride(0), _code(a.dtype), M, K, _ptr(positions),
+        _ptr(cos_tab), _ptr(sin_tab), cos_tab.shape[0], H, KV, D, _ptr(q_out), _ptr(k_cache),
+        _ptr(v_cache), n_ctx, _stream(stream)))
+    return q_out

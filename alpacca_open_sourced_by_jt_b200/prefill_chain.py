@@ -13,8 +13,8 @@ straight into a DecodeChain's caches, so decoding continues from it:
   embed rows              b2a_q8_embed (all T tokens)
   per layer:
     h    = RMSNorm(x)      b2a_rmsnorm_rows, written as the cache's 16-bit type
-    qkv  = h . Wqkv^T      b2a_gemm (tcgen05), f32 out
-    RoPE + K/V append, q rotated to 16 bits           b2a_rope_append
+    q, k, v = h . Wqkv^T, RoPE, K/V rows appended, q rotated to 16 bits
+                           b2a_gemm_qkv_rope (tcgen05, all in the epilogue)
     att  = causal prefill over cache rows 0..pos0+T-1  b2a_prefill (tcgen05)
     x   += att . Wo^T      b2a_gemm, the residual added in its epilogue, in place
     h    = RMSNorm(x)      b2a_rmsnorm_rows
@@ -63,7 +63,6 @@ class ChunkPrefill:
                   for ly in m.layers]
         T, E, H, KV, D, F = self.max_chunk, m.E, m.H, m.KV, m.D, m.F
         self.x = torch.zeros((T, E), dtype=torch.float32, device=dev)
-        self.qkv = torch.zeros((T, (H + 2 * KV) * D), dtype=torch.float32, device=dev)
         self.h = torch.zeros((T, E), dtype=dt, device=dev)
         self.qrot = torch.zeros((T, H, D), dtype=dt, device=dev)
         self.att = torch.zeros((T, H, D), dtype=dt, device=dev)
@@ -102,7 +101,7 @@ class ChunkPrefill:
         if toks.min() < 0 or toks.max() >= m.V:
             raise _lib.B2AError(_lib.ERR_ARG, "token id outside the vocabulary")
         H, KV, D, E = m.H, m.KV, m.D, m.E
-        qd, kd = H * D, KV * D
+        qd = H * D
         lib = _lib.load()
         st = device._stream(None)
         self.tokens[:T].copy_(torch.from_numpy(toks))
@@ -114,12 +113,9 @@ class ChunkPrefill:
         t_kv = pos0 + T
         for li, (ly, w) in enumerate(zip(m.layers, self.w)):
             h = self._norm(x, ly["attn_norm"], T)
-            qkv = device.gemm(h, w["qkv"], out=self.qkv[:T])
-            q = qkv[:, :qd].view(T, H, D)
-            k = qkv[:, qd:qd + kd].view(T, KV, D)
-            v = qkv[:, qd + kd:].view(T, KV, D)
-            device.rope_append(q, k, v, pos, ch.cos, ch.sin, k_cache=ch.k_cache[li],
-                               v_cache=ch.v_cache[li], q_out=self.qrot[:T])
+            device.gemm_qkv_rope(h, w["qkv"], pos, ch.cos, ch.sin, H=H, KV=KV,
+                                 k_cache=ch.k_cache[li], v_cache=ch.v_cache[li],
+                                 q_out=self.qrot[:T])
             att = device.prefill(self.qrot[:T], ch.k_cache[li][0, :t_kv],
                                  ch.v_cache[li][0, :t_kv], pos, out=self.att[:T])
             device.gemm(att.view(T, qd), w["wo"], out=x, c_in=x)

@@ -603,8 +603,8 @@ def bench_prefill_chunk(dev, steps, warmup):
                          "peak_source": f"{src} (MEASURED_PEAKS.json bf16_tflops, burst)"},
             "config": "16 layers, hidden 2048, 32/8 heads x 64, FFN 8192, vocab 128256; "
                       "weights dequantized to f16; every kernel this library's: tcgen05 GEMMs "
-                      "(residual add and SwiGLU in their epilogues), RMSNorm, RoPE+append, "
-                      "tcgen05 causal prefill; eager launches (8 per layer)"}
+                      "(RoPE + K/V append, residual add and SwiGLU in their epilogues), RMSNorm, "
+                      "tcgen05 causal prefill; eager launches (7 per layer)"}
 
 
 def bench_e2e(dev, st, steps, warmup):

@@ -70,7 +70,7 @@ int b2a_device_error(int* code, int* aux, int clear);
 
 /* Launch mode of the calling thread's later launches; returns the previous
  * flags.  B2A_LAUNCH_PDL launches b2a_rope_append, b2a_imrope_append,
- * b2a_decode (both kernels), b2a_lse_combine and b2a_gemm as
+ * b2a_decode (both kernels), b2a_lse_combine, b2a_gemm and b2a_gemm_qkv_rope as
  * programmatic dependents of the kernel before them on the stream: each
  * starts while that kernel drains and waits for it (griddepcontrol.wait)
  * before reading what it wrote.  The decode's K/V rows below the newest
@@ -351,6 +351,23 @@ int b2a_swiglu_rows(const float* gu, long long gu_row_stride, int interleaved, v
 int b2a_gemm(const void* a, long long lda, const void* w, long long ldw, int dtype,
              const float* c_in, long long ldc, void* out, long long ldo, int out_dtype, int M,
              int N, int K, int epilogue, void* stream);
+
+/* A prefill chunk's QKV projection with RoPE and the K/V append in the
+ * epilogue: the tcgen05 GEMM of b2a_gemm over the (H + 2*KV)*D rows
+ * [q; k; v] of w (a [M][lda], w [N][ldw], both of dtype F16 or BF16), then
+ * for each token row m at position pos_dev[m] (model.py:1303-1337; device
+ * prefill_chunk, cuda.py:1943-2080 with _rope_store_batch, cuda.py:885-953):
+ *   q  rotated (norm style: pairs 2i, 2i+1 of each head, the reference's
+ *      f32 products) into q_out [M][H*D] of dtype
+ *   k  rotated into k_cache row pos ([n_ctx][KV][D] of dtype)
+ *   v  into v_cache row pos
+ * cos_tab / sin_tab f32 [tab_rows][D/2]; D a multiple of 32.  A position
+ * outside the cache or table records B2A_ERR_POSITION and writes nothing
+ * for that token.  One launch instead of b2a_gemm plus b2a_rope_append. */
+int b2a_gemm_qkv_rope(const void* a, long long lda, const void* w, long long ldw, int dtype,
+                      int M, int K, const int* pos_dev, const float* cos_tab, const float* sin_tab,
+                      int tab_rows, int H, int KV, int D, void* q_out, void* k_cache,
+                      void* v_cache, int n_ctx, void* stream);
 
 #ifdef __cplusplus
 }

@@ -111,3 +111,52 @@ def test_gemm_rejects_bad_arguments(cuda_dev):
     lib = _lib.load()
     assert lib.b2a_gemm(a.data_ptr(), 60, w.data_ptr(), 64, _lib.BF16, None, 0,
                         a.data_ptr(), 64, _lib.F32, 16, 256, 64, 0, None) == _lib.ERR_ALIGN
+
+
+@pytest.mark.parametrize("T,E,H,KV,D,pos0", [(200, 512, 8, 2, 128, 37), (77, 320, 4, 4, 64, 0),
+                                             (256, 4096, 32, 8, 128, 1000)])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_gemm_qkv_rope_equals_gemm_then_rope(cuda_dev, T, E, H, KV, D, pos0, dt):
+    """The fused epilogue gives what the two launches give, bit for bit: the
+    same fp32 accumulator, rotated with the same rounded products and stored
+    with the same rounding."""
+    from alpacca_open_sourced_by_jt_b200 import device
+    g = torch.Generator(device=cuda_dev).manual_seed(T + E)
+    n_ctx = pos0 + T + 5
+    a = torch.randn((T, E), device=cuda_dev, generator=g).to(dt)
+    w = (0.05 * torch.randn(((H + 2 * KV) * D, E), device=cuda_dev, generator=g)).to(dt)
+    cos, sin = device.rope_tables(n_ctx, D, 10000.0, device=cuda_dev)
+    pos = torch.arange(pos0, pos0 + T, dtype=torch.int32, device=cuda_dev)
+    kc0, vc0 = (torch.zeros((1, n_ctx, KV, D), device=cuda_dev, dtype=dt) for _ in range(2))
+    q0 = torch.zeros((T, H, D), device=cuda_dev, dtype=dt)
+    qkv = device.gemm(a, w)
+    qd, kd = H * D, KV * D
+    device.rope_append(qkv[:, :qd].view(T, H, D), qkv[:, qd:qd + kd].view(T, KV, D),
+                       qkv[:, qd + kd:].view(T, KV, D), pos, cos, sin, k_cache=kc0,
+                       v_cache=vc0, q_out=q0)
+    kc1, vc1 = torch.zeros_like(kc0), torch.zeros_like(vc0)
+    q1 = torch.zeros_like(q0)
+    device.gemm_qkv_rope(a, w, pos, cos, sin, H=H, KV=KV, k_cache=kc1, v_cache=vc1, q_out=q1)
+    torch.cuda.synchronize()
+    assert torch.equal(q1, q0)
+    assert torch.equal(kc1, kc0) and torch.equal(vc1, vc0)
+    assert kc1[0, pos0 + T:].abs().sum().item() == 0
+
+
+def test_gemm_qkv_rope_position_outside_cache(cuda_dev):
+    from alpacca_open_sourced_by_jt_b200 import _lib, device
+    _lib.device_error(clear=True)
+    n_ctx, H, KV, D, E = 16, 2, 1, 64, 128
+    a = torch.randn((2, E), device=cuda_dev).to(torch.bfloat16)
+    w = torch.randn(((H + 2 * KV) * D, E), device=cuda_dev).to(torch.bfloat16)
+    cos, sin = device.rope_tables(n_ctx, D, 10000.0, device=cuda_dev)
+    kc = torch.zeros((n_ctx, KV, D), device=cuda_dev, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    q = torch.zeros((2, H, D), device=cuda_dev, dtype=torch.bfloat16)
+    pos = torch.tensor([3, n_ctx], dtype=torch.int32, device=cuda_dev)  # second is out of range
+    device.gemm_qkv_rope(a, w, pos, cos, sin, H=H, KV=KV, k_cache=kc, v_cache=vc, q_out=q)
+    code, aux = _lib.device_error(clear=True)
+    assert code == _lib.ERR_POSITION and aux == 1
+    assert kc[3].abs().sum().item() > 0 and q[0].abs().sum().item() > 0
+    assert q[1].abs().sum().item() == 0
+    assert kc[4:].abs().sum().item() == 0 and vc[4:].abs().sum().item() == 0
