@@ -18,9 +18,10 @@
 // (16-bit) plus the rotated k and the v rows at each token's cache position,
 // the work of b2a_rope_append, from the fp32 accumulator.
 //
-// Kernel: persistent, one CTA per SM, 128 x 256 output tiles taken in
-// m-fastest order (the CTAs working at one time share a weight tile, which
-// then comes from L2).  256 threads:
+// Kernel: persistent, one CTA per SM, 128 x 256 output tiles (128 x 192
+// where that takes fewer tile-widths of waves) taken in m-fastest order (the
+// CTAs working at one time share a weight tile, which then comes from L2).
+// 256 threads:
 //   warp 0       TMA producer: A (128 x 64) and W (256 x 64) K-blocks into a
 //                4-stage ring of 48 KB stages (128-byte swizzle)
 //   warp 1       TMEM owner, single-lane MMA issuer: 4 x tcgen05.mma
@@ -47,10 +48,10 @@ constexpr int kBM = 128, kBN = 256, kBK = 64;
 constexpr int kStages = 4;
 constexpr int kThreads = 256;
 constexpr int kABytes = kBM * kBK * 2;  // 16 KB
-constexpr int kWBytes = kBN * kBK * 2;  // 32 KB
-constexpr int kStageBytes = kABytes + kWBytes;
-constexpr int kSmem = kStages * kStageBytes + 1024;
-constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
+// A stage is the A block plus a BN x 64 weight block (32 KB at BN = 256)
+constexpr int smem_for(int bn) { return kStages * (kABytes + bn * kBK * 2) + 1024; }
+constexpr uint32_t kTmemCols = 512;  // two accumulators of up to 256 columns
+constexpr uint32_t kAccStride = 256;
 
 template <typename TO>
 __device__ __forceinline__ void store32(TO* dst, const float* v);
@@ -102,11 +103,14 @@ struct QkvRope {
   int tab_rows, n_ctx, H, KV, D;
 };
 
-template <typename T, typename TO, int Epi>
+template <typename T, typename TO, int Epi, int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
     const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
     const float* __restrict__ c_in, long long ldc, TO* __restrict__ out, long long ldo, int M,
     int N, int K, const QkvRope rp) {
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256 && (Epi != 1 || BN == 256),
+                "tile width: 64..256 columns, 256 for the SwiGLU halves");
+  constexpr int kStage = kABytes + BN * kBK * 2;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_full[kStages], bar_empty[kStages];
   __shared__ __align__(8) uint64_t bar_acc_full[2], bar_acc_empty[2];
@@ -114,7 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mt = (M + kBM - 1) / kBM, nt = (N + kBN - 1) / kBN;
+  const int mt = (M + kBM - 1) / kBM, nt = (N + BN - 1) / BN;
   const int n_tiles = mt * nt;
   const int nk = (K + kBK - 1) / kBK;
 
@@ -152,7 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
       uint32_t it = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x) {
-        const int m0 = (t % mt) * kBM, n0 = (t / mt) * kBN;
+        const int m0 = (t % mt) * kBM, n0 = (t / mt) * BN;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % kStages;
           if (it >= kStages &&
@@ -160,8 +164,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&bar_full[s], kStageBytes);
-          uint8_t* sa = smem + s * kStageBytes;
+          mbar_arrive_expect_tx(&bar_full[s], kStage);
+          uint8_t* sa = smem + s * kStage;
           asm volatile(
               "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
               " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(sa)),
@@ -180,10 +184,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------ MMA issuer ---------------------------
-      constexpr uint32_t idesc = make_idesc<T>(kBM, kBN, false, false);
+      constexpr uint32_t idesc = make_idesc<T>(kBM, BN, false, false);
       const uint64_t dA0 = sw128_desc(smem_u32(smem), 16, 1024);
       const uint64_t dW0 = sw128_desc(smem_u32(smem + kABytes), 16, 1024);
-      constexpr uint64_t kStageStep = kStageBytes >> 4;
+      constexpr uint64_t kStageStep = kStage >> 4;
       uint32_t it = 0, tc = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++tc) {
@@ -194,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
           break;
         }
         tc_fence_after();
-        const uint32_t acc = tmem + b * kBN;
+        const uint32_t acc = tmem + b * kAccStride;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % kStages;
           if (!mbar_wait(&bar_full[s], (it / kStages) & 1, 0x33000 | (kb & 0xfff))) {
@@ -222,10 +226,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
                                 mbar_wait(&bar_acc_full[b], (tc >> 1) & 1, 0x34000 | (tc & 0xfff)));
       if (!w) break;
       tc_fence_after();
-      const int m0 = (t % mt) * kBM, n0 = (t / mt) * kBN;
+      const int m0 = (t % mt) * kBM, n0 = (t / mt) * BN;
       const int row = m0 + q * 32 + lane;
       const bool rv = row < M;
-      const uint32_t acc = tl + b * kBN;
+      const uint32_t acc = tl + b * kAccStride;
       if (Epi == 0) {
         // the residual of chunk c + 1 is in flight while chunk c is added and
         // stored (one global round trip per tile instead of one per chunk)
@@ -237,10 +241,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
           for (int i = 0; i < 8; ++i) rc[i] = *reinterpret_cast<const float4*>(crow + n0 + 4 * i);
         }
 #pragma unroll
-        for (int c = 0; c < kBN / 32; ++c) {
+        for (int c = 0; c < BN / 32; ++c) {
           float v[32];
           tc_ld32(acc + c * 32, v);
-          if (c + 1 < kBN / 32 && c_in && full(c + 1)) {
+          if (c + 1 < BN / 32 && c_in && full(c + 1)) {
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               rn[i] = *reinterpret_cast<const float4*>(crow + n0 + (c + 1) * 32 + 4 * i);
@@ -289,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
           }
         }
 #pragma unroll 1
-        for (int c = 0; c < kBN / 32; ++c) {
+        for (int c = 0; c < BN / 32; ++c) {
           const int col = n0 + c * 32;
           if (col >= N) break;
           float v[32];
@@ -331,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
       } else {
         // SwiGLU: columns [0,128) of the tile are gate rows, [128,256) the up rows
 #pragma unroll 1
-        for (int c = 0; c < kBN / 64; ++c) {
+        for (int c = 0; c < BN / 64; ++c) {
           float g[32], u[32];
           tc_ld32(acc + c * 32, g);
           tc_ld32(acc + 128 + c * 32, u);
@@ -365,12 +369,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
 // ===========================================================================
 namespace {
 
-template <typename T, typename TO, int Epi>
+template <typename T, typename TO, int Epi, int BN = 256>
 int launch_gemm(const void* a, long long lda, const void* w, long long ldw, const float* c_in,
                 long long ldc, void* out, long long ldo, int M, int N, int K, cudaStream_t st,
                 const b2a::gemm::QkvRope& rp = b2a::gemm::QkvRope{}) {
   namespace G = b2a::gemm;
-  auto kern = G::gemm_kernel<T, TO, Epi>;
+  auto kern = G::gemm_kernel<T, TO, Epi, BN>;
   const CUtensorMapDataType tdt = std::is_same<T, __nv_bfloat16>::value
                                       ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -380,25 +384,50 @@ int launch_gemm(const void* a, long long lda, const void* w, long long ldw, cons
   const uint64_t wdims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
   const uint64_t wstr[1] = {static_cast<uint64_t>(ldw) * 2};
   const uint32_t abox[2] = {static_cast<uint32_t>(G::kBK), static_cast<uint32_t>(G::kBM)};
-  const uint32_t wbox[2] = {static_cast<uint32_t>(G::kBK), static_cast<uint32_t>(G::kBN)};
+  const uint32_t wbox[2] = {static_cast<uint32_t>(G::kBK), static_cast<uint32_t>(BN)};
   int rc = b2a_host::make_tmap(&ta, tdt, 2, const_cast<void*>(a), adims, astr, abox,
                                CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = b2a_host::make_tmap(&tw, tdt, 2, const_cast<void*>(w), wdims, wstr, wbox,
                            CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  constexpr int smem_bytes = G::kSmem;
+  constexpr int smem_bytes = G::smem_for(BN);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "cudaFuncSetAttribute(gemm)");
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int tiles = ((M + G::kBM - 1) / G::kBM) * ((N + G::kBN - 1) / G::kBN);
+  const int tiles = ((M + G::kBM - 1) / G::kBM) * ((N + BN - 1) / BN);
   const int grid = tiles < sms ? tiles : sms;
   e = b2a_host::launch(kern, dim3(grid), dim3(G::kThreads), smem_bytes, st, ta, tw, c_in, ldc,
                        static_cast<TO*>(out), ldo, M, N, K, rp);
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "gemm launch");
   return B2A_OK;
+}
+
+// 192-column tiles where they need fewer tile-widths of waves than 256:
+// (waves of tiles over the SMs) x (tile width); e.g. 2048 x 3072 on 148
+// SMs is 2 x 192 against 2 x 256, 2048 x 2048 is 2 x 192 against 1 x 256
+bool narrow_tiles(int M, int N) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  auto cost = [&](int bn) {
+    const long long tiles = static_cast<long long>((M + 127) / 128) * ((N + bn - 1) / bn);
+    return (tiles + sms - 1) / sms * bn;
+  };
+  return cost(192) < cost(256);
+}
+
+template <typename T, typename TO, int Epi>
+int launch_gemm_auto(const void* a, long long lda, const void* w, long long ldw,
+                     const float* c_in, long long ldc, void* out, long long ldo, int M, int N,
+                     int K, cudaStream_t st,
+                     const b2a::gemm::QkvRope& rp = b2a::gemm::QkvRope{}) {
+  if (Epi != 1 && narrow_tiles(M, N))
+    return launch_gemm<T, TO, Epi, (Epi == 1 ? 256 : 192)>(a, lda, w, ldw, c_in, ldc, out, ldo, M,
+                                                           N, K, st, rp);
+  return launch_gemm<T, TO, Epi, 256>(a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st, rp);
 }
 
 template <typename T, int Epi>
@@ -407,11 +436,12 @@ int gemm_out(int out_dtype, const void* a, long long lda, const void* w, long lo
              cudaStream_t st) {
   switch (out_dtype) {
     case B2A_F32:
-      return launch_gemm<T, float, Epi>(a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
+      return launch_gemm_auto<T, float, Epi>(a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
     case B2A_F16:
-      return launch_gemm<T, __half, Epi>(a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
+      return launch_gemm_auto<T, __half, Epi>(a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
     case B2A_BF16:
-      return launch_gemm<T, __nv_bfloat16, Epi>(a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
+      return launch_gemm_auto<T, __nv_bfloat16, Epi>(a, lda, w, ldw, c_in, ldc, out, ldo, M, N,
+                                                     K, st);
   }
   return b2a_host::fail(B2A_ERR_DTYPE, "gemm: out_dtype %d", out_dtype);
 }
@@ -477,10 +507,11 @@ int b2a_gemm_qkv_rope(const void* a, long long lda, const void* w, long long ldw
                               tab_rows, n_ctx, H, KV, D};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == B2A_BF16)
-    return launch_gemm<__nv_bfloat16, __nv_bfloat16, 2>(a, lda, w, ldw, nullptr, 0, nullptr, 0, M,
-                                                        N, K, st, rp);
+    return launch_gemm_auto<__nv_bfloat16, __nv_bfloat16, 2>(a, lda, w, ldw, nullptr, 0, nullptr,
+                                                             0, M, N, K, st, rp);
   if (dtype == B2A_F16)
-    return launch_gemm<__half, __half, 2>(a, lda, w, ldw, nullptr, 0, nullptr, 0, M, N, K, st, rp);
+    return launch_gemm_auto<__half, __half, 2>(a, lda, w, ldw, nullptr, 0, nullptr, 0, M, N, K, st,
+                                               rp);
   return fail(B2A_ERR_DTYPE, "gemm_qkv_rope: dtype %d (f16 or bf16)", dtype);
 }
 

@@ -507,8 +507,9 @@ def bench_decode_step(dev, steps, warmup):
 
 def bench_gemm(dev, steps, warmup):
     """The prefill chunk's projections (b2a_gemm, tcgen05) at the config-5 shapes for a
-    2048-token chunk, each with the epilogue the chunk uses (QKV fp32 out, Wo and down
-    with the residual added in place, gate/up with SwiGLU writing f16), timed by CUDA
+    2048-token chunk, each with the epilogue the chunk uses (QKV with RoPE and the K/V
+    append, Wo and down with the residual added in place, gate/up with SwiGLU writing
+    f16), timed by CUDA
     events; beside each, PyTorch's 16-bit GEMM with fp32 output (cuBLAS) on the same
     operands without the fused work.  Bound: tensor cores."""
     import torch
@@ -516,7 +517,7 @@ def bench_gemm(dev, steps, warmup):
     T, E, F = 2048, C5["n_embd"], C5["n_ff"]
     qkv_n = (C5["n_head"] + 2 * C5["n_kv"]) * C5["head_dim"]
     g = torch.Generator(device=dev).manual_seed(7)
-    shapes = (("qkv", qkv_n, E, "store"), ("wo", E, E, "residual"),
+    shapes = (("qkv", qkv_n, E, "rope"), ("wo", E, E, "residual"),
               ("gate_up", 2 * F, E, "swiglu"), ("down", E, F, "residual"))
     n = max(3, min(steps, 20))
 
@@ -543,6 +544,15 @@ def bench_gemm(dev, steps, warmup):
         elif epi == "residual":
             o = torch.zeros((T, N), device=dev)
             fn = lambda: device.gemm(a, w, out=o, c_in=o)
+        elif epi == "rope":
+            H, KV, D = C5["n_head"], C5["n_kv"], C5["head_dim"]
+            cos, sin = device.rope_tables(T, D, 10000.0, device=dev)
+            pos = torch.arange(T, dtype=torch.int32, device=dev)
+            kc = torch.zeros((T, KV, D), device=dev, dtype=torch.float16)
+            vc = torch.zeros_like(kc)
+            o = torch.empty((T, H, D), device=dev, dtype=torch.float16)
+            fn = lambda: device.gemm_qkv_rope(a, w, pos, cos, sin, H=H, KV=KV, k_cache=kc,
+                                              v_cache=vc, q_out=o)
         else:
             o = torch.empty((T, N), device=dev)
             fn = lambda: device.gemm(a, w, out=o)
