@@ -5,8 +5,9 @@
 //
 // HBM-bound: each element is read once and written once.  Each thread moves
 // 8 elements per step with 16-byte (16-bit side) or 2 x 16-byte (f32 side)
-// accesses when both buffers are 16-byte aligned; the grid is a multiple of
-// the SM count and strides over the buffer.  Narrowing rounds to nearest
+// accesses when both buffers are 16-byte aligned (widening: two steps' loads
+// before their stores); the grid is a multiple of the SM count and strides
+// over the buffer.  Narrowing rounds to nearest
 // even (__float2half_rn / __float2bfloat16_rn), as NumPy's astype(float16)
 // and torch's bfloat16 cast do.
 
@@ -54,10 +55,26 @@ __global__ void __launch_bounds__(kThreads) convert_kernel(const S* __restrict__
   const long long nthreads = static_cast<long long>(gridDim.x) * blockDim.x;
   long long done = 0;
   if (vector_ok) {
+    // widening writes twice what it reads: two loads in flight per thread
+    // before the stores keep more reads queued behind the write stream
+    constexpr int U = sizeof(Dt) > sizeof(S) ? 2 : 1;
     const long long nv = n / kVec;
     const Vec8<S>* sv = reinterpret_cast<const Vec8<S>*>(src);
     Vec8<Dt>* dv = reinterpret_cast<Vec8<Dt>*>(dst);
-    for (long long i = tid; i < nv; i += nthreads) {
+    long long i = tid;
+    for (; U > 1 && i + (U - 1) * nthreads < nv; i += U * nthreads) {
+      Vec8<S> a[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) a[u] = sv[i + u * nthreads];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        Vec8<Dt> b;
+#pragma unroll
+        for (int k = 0; k < kVec; ++k) b.e[k] = cvt<S, Dt>(a[u].e[k]);
+        dv[i + u * nthreads] = b;
+      }
+    }
+    for (; i < nv; i += nthreads) {
       const Vec8<S> a = sv[i];
       Vec8<Dt> b;
 #pragma unroll
@@ -81,7 +98,8 @@ int launch_convert(const void* src, void* dst, long long n, cudaStream_t st) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const long long per_block = static_cast<long long>(b2a::kv::kThreads) * b2a::kv::kVec;
   long long blocks = (n + per_block - 1) / per_block;
-  const long long cap = static_cast<long long>(sms) * 8;  // 8 x 256 threads per SM
+  // 8 x 256 threads resident per SM; widening launches two rounds of them
+  const long long cap = static_cast<long long>(sms) * (sizeof(Dt) > sizeof(S) ? 16 : 8);
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   const int vec = b2a_host::aligned16(src) && b2a_host::aligned16(dst) &&
