@@ -40,7 +40,12 @@ def test_version(lib):
 
 def test_workspace_and_split_helpers(lib):
     sr = lib.b2a_decode_split_rows(16, 8, 32768, _lib.BF16)
-    assert sr % 64 == 0 and 256 <= sr <= 2048
+    assert sr % 64 == 0 and 256 <= sr <= 8192
+    # every sequence of max_len keeps at least 4 splits, and no split is under 256 rows
+    for args in ((16, 8, 32768), (64, 8, 8192), (4, 8, 131072), (1, 8, 4096), (2, 2, 512)):
+        s = lib.b2a_decode_split_rows(*args, _lib.BF16)
+        assert s % 64 == 0 and 256 <= s <= 8192
+        assert s == 256 or 4 * s <= args[2]
     n_split = -(-32768 // sr)
     ws = lib.b2a_decode_workspace_bytes(16, 32, 128, 32768, sr)
     assert ws >= 16 * 32 * n_split * (128 + 2) * 4
