@@ -234,6 +234,10 @@ bool aligned16(const void* p);
 // The calling thread's b2a_set_launch_flags value.
 int launch_flags();
 
+// Number of SMs of the current device (cudaDevAttrMultiProcessorCount, read
+// once per device and cached), for persistent grids and split heuristics.
+int sm_count();
+
 // Launch `kern`, as a programmatic dependent of the stream's previous kernel
 // when the thread's launch flags ask for it (the kernel then waits with
 // griddepcontrol.wait before reading that kernel's output).

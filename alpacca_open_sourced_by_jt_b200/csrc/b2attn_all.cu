@@ -6,6 +6,7 @@
 #include "prefill.cu"
 #include "prefill_pair.cu"
 #include "prefill_head.cu"
+#include "prefill_f32.cu"
 #include "gemm.cu"
 #include "kvconvert.cu"
 #include "qwen35_layer.cu"

@@ -575,8 +575,6 @@ using Dk::kCombineThreads;
 using Dk::smem_bytes;
 using b2a_host::fail;
 
-constexpr int kNumSMs = 148;
-
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 int n_splits_of(int max_len, int split_rows) {
@@ -682,7 +680,7 @@ int b2a_decode_split_rows(int B, int KV, int max_len, int kv_dtype) {
   if (B <= 0 || KV <= 0 || max_len <= 0) return kRows * 4;
   const double rows_total = static_cast<double>(B) * KV * max_len;
   int sr = kRows;
-  while (sr < 8192 && 8LL * sr <= max_len && rows_total / sr > kNumSMs) sr *= 2;
+  while (sr < 8192 && 8LL * sr <= max_len && rows_total / sr > b2a_host::sm_count()) sr *= 2;
   if (sr < 4 * kRows) sr = 4 * kRows;
   return sr;
 }
@@ -817,24 +815,52 @@ constexpr size_t kNoAllocScratchBytes = B2A_DECODE_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
 
 std::mutex g_scratch_mu;
-void* g_scratch_addr[64] = {};  // device address of g_decode_scratch, per device
+struct ScratchSlot {
+  void* ctx;   // CUDA context the address belongs to
+  void* addr;  // device address of g_decode_scratch in that context
+};
+ScratchSlot g_scratch_addr[64] = {};  // per device ordinal
+
+typedef CUresult (*PFN_ctxGetCurrent)(CUcontext*);
+
+// The calling thread's current CUDA context (driver entry point, no -lcuda
+// link); null if it cannot be read.
+void* current_context() {
+  static PFN_ctxGetCurrent fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_ctxGetCurrent>(p);
+  });
+  CUcontext c = nullptr;
+  if (!fn || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
 
 // Device address of the scratch array on the current device. The host-side
-// name g_decode_scratch is only a stand-in, so the address is looked up once
-// per device with that device current.
+// name g_decode_scratch is only a stand-in, so the address is looked up with
+// that device current, once per device and context: a context made after
+// cudaDeviceReset (which reloads the module) gets a fresh lookup.
 int scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "decode_noalloc: cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(B2A_ERR_UNSUPPORTED, "decode_noalloc: device %d >= 64", dev);
+  void* ctx = current_context();  // null before the runtime made one
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_addr[dev]) {
+  ScratchSlot& slot = g_scratch_addr[dev];
+  if (!slot.addr || !ctx || slot.ctx != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_decode_scratch);
-    if (e != cudaSuccess || !p) return b2a_host::cuda_fail(e, "decode_noalloc: cudaGetSymbolAddress");
-    g_scratch_addr[dev] = p;
+    if (e != cudaSuccess) return b2a_host::cuda_fail(e, "decode_noalloc: cudaGetSymbolAddress");
+    if (!p) return fail(B2A_ERR_CUDA, "decode_noalloc: cudaGetSymbolAddress returned a null address");
+    slot.ctx = current_context();  // the lookup made the context if there was none
+    slot.addr = p;
   }
-  *out = g_scratch_addr[dev];
+  *out = slot.addr;
   return B2A_OK;
 }
 

@@ -174,6 +174,40 @@ struct Pack2<__half> {
 namespace b2a {
 namespace prefill {
 
+// A query row with no visible key gets the mean of all t_kv value rows of
+// its KV head: the NumPy path masks with -1e30, so every key of such a row
+// has weight exp(0) / t_kv (alpaccaroo/model.py:1266-1270, 1584-1588).
+// Warp-cooperative: every lane takes part; the rows of the lanes with
+// `need` set are written, the lanes splitting the columns (D <= 256).
+// Only degenerate inputs (a position before every cached key, or a window
+// that excludes them all) reach the loop, so it favours simplicity.
+template <typename T, typename TO>
+__device__ __noinline__ void store_mean_v_rows(bool need, TO* orow, const T* __restrict__ v,
+                                               int t_kv, int KV, int kvh, int D) {
+  unsigned mask = __ballot_sync(0xffffffffu, need);
+  if (mask == 0u) return;
+  const int lane = threadIdx.x & 31;
+  float acc[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+  for (int s = 0; s < t_kv; ++s) {
+    const T* vr = v + (static_cast<size_t>(s) * KV + kvh) * D;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      if (lane + 32 * c < D) acc[c] += ld_elem(vr + lane + 32 * c);
+  }
+  const float inv = 1.f / static_cast<float>(t_kv);
+  while (mask) {
+    const int r = __ffs(mask) - 1;
+    mask &= mask - 1u;
+    TO* dst = reinterpret_cast<TO*>(
+        __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(orow), r));
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      if (lane + 32 * c < D) st_elem(dst + lane + 32 * c, acc[c] * inv);
+  }
+}
+
 template <typename TO>
 __device__ __forceinline__ void store_row32(TO* dst, const float* v, float scale);
 template <>
@@ -212,8 +246,9 @@ __device__ __forceinline__ void store_row32<__half>(__half* dst, const float* v,
 template <typename T, typename TO, int D>
 __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-    const __grid_constant__ CUtensorMap tmV, const int* __restrict__ pos, TO* __restrict__ out,
-    int n_q, int t_kv, int H, int group, int n_q_tiles, float sscale, int window, int kv_start) {
+    const __grid_constant__ CUtensorMap tmV, const T* __restrict__ vraw, const int* __restrict__ pos,
+    TO* __restrict__ out, int n_q, int t_kv, int H, int group, int n_q_tiles, float sscale,
+    int window, int kv_start) {
   using L = Layout<D>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_q;
@@ -468,8 +503,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = 0.f;
       }
-      if (t < n_q) store_row32<TO>(orow + c * 32, o, inv);
+      if (t < n_q && l > 0.f) store_row32<TO>(orow + c * 32, o, inv);
     }
+    store_mean_v_rows<T, TO>(ok && t < n_q && !(l > 0.f), orow, vraw, t_kv, H / group, kvh, D);
   }
   // ------------------------------ teardown ---------------------------------
   tc_fence_before();
@@ -494,22 +530,28 @@ using P::kBM;
 using P::prefill_kernel;
 using b2a_host::fail;
 
-// Defined in prefill_pair.cu (same translation unit).
+// Defined in prefill_pair.cu, prefill_head.cu and prefill_f32.cu (same
+// translation unit).
 template <typename T, typename TO, int D>
 int launch_prefill_pair(const void* q, const void* k, const void* v, const int* pos, void* out,
                         int n_q, int t_kv, int H, int KV, float scale, int window, int kv_start,
                         cudaStream_t st);
 
 template <typename T, typename TO, int D>
-int launch_prefill_head(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                        const int* pos, void* out, int n_q, int t_kv, int H, int KV, float scale,
-                        int window, int kv_start, cudaStream_t st);
+int launch_prefill_head(const void* q, const void* k, const void* v, const int* pos, void* out,
+                        int n_q, int t_kv, int H, int KV, float scale, int window, int kv_start,
+                        cudaStream_t st);
 
-// Kernel choice.  Default: the paired-head persistent kernel
-// (prefill_pair.cu) for even GQA groups, the one-head persistent kernel
-// (prefill_head.cu) otherwise.  B2ATTN_PREFILL=head|pair|single forces one
-// (pair falls back to head for odd groups); the non-persistent one-tile
-// kernel below is kept as a tested reference schedule.
+int prefill_f32_dispatch(int out_dtype, const void* q, const void* k, const void* v,
+                         const int* pos, void* out, int n_q, int t_kv, int H, int KV, int D,
+                         float scale, int window, int kv_start, cudaStream_t st);
+
+// Kernel choice for 16-bit inputs.  Default: the paired-head persistent
+// kernel (prefill_pair.cu) for even GQA groups at head_dim 64 and 128, the
+// one-head persistent kernel (prefill_head.cu) otherwise and always at
+// head_dim 256.  B2ATTN_PREFILL=head|pair|single forces one where it serves
+// the shape (pair falls back to head for odd groups); the non-persistent
+// one-tile kernel below is kept as a tested reference schedule.
 enum class PrefillKernel { kHead, kPair, kSingle };
 PrefillKernel prefill_choice(int group) {
   const char* e = getenv("B2ATTN_PREFILL");
@@ -521,41 +563,47 @@ PrefillKernel prefill_choice(int group) {
 template <typename T, typename TO, int D>
 int launch_prefill(const void* q, const void* k, const void* v, const int* pos, void* out, int n_q,
                    int t_kv, int H, int KV, float scale, int window, int kv_start, cudaStream_t st) {
-  const PrefillKernel choice = prefill_choice(H / KV);
-  if (choice == PrefillKernel::kPair && (H / KV) % 2 == 0)
-    return launch_prefill_pair<T, TO, D>(q, k, v, pos, out, n_q, t_kv, H, KV, scale, window,
+  if constexpr (D > 128) {
+    return launch_prefill_head<T, TO, D>(q, k, v, pos, out, n_q, t_kv, H, KV, scale, window,
                                          kv_start, st);
-  const CUtensorMapDataType tdt = std::is_same<T, __nv_bfloat16>::value
-                                      ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUtensorMap tq, tk, tv;
-  const uint64_t qdims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(H), static_cast<uint64_t>(n_q)};
-  const uint64_t qstr[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(H) * D * 2};
-  const uint64_t kdims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(KV), static_cast<uint64_t>(t_kv)};
-  const uint64_t kstr[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(KV) * D * 2};
-  const uint32_t box[3] = {64, 1, 128};
-  int rc = b2a_host::make_tmap(&tq, tdt, 3, const_cast<void*>(q), qdims, qstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
-  rc = b2a_host::make_tmap(&tk, tdt, 3, const_cast<void*>(k), kdims, kstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
-  rc = b2a_host::make_tmap(&tv, tdt, 3, const_cast<void*>(v), kdims, kstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
-  if (choice == PrefillKernel::kHead)
-    return launch_prefill_head<T, TO, D>(tq, tk, tv, pos, out, n_q, t_kv, H, KV, scale, window,
-                                         kv_start, st);
-  auto kern = prefill_kernel<T, TO, D>;
-  // >= 116 KB keeps one CTA per SM, so the 512-column TMEM allocation never
-  // waits on a co-resident CTA.
-  const int smem = Layout<D>::kSmem > 116 * 1024 ? Layout<D>::kSmem : 116 * 1024;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return b2a_host::cuda_fail(e, "cudaFuncSetAttribute(prefill)");
-  const int n_q_tiles = (n_q + kBM - 1) / kBM;
-  dim3 grid(n_q_tiles, H);
-  kern<<<grid, P::kThreads, smem, st>>>(tq, tk, tv, pos, static_cast<TO*>(out), n_q, t_kv, H, H / KV,
-                                     n_q_tiles, scale * P::kLog2e, window, kv_start);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return b2a_host::cuda_fail(e, "prefill launch");
-  return B2A_OK;
+  } else {
+    const PrefillKernel choice = prefill_choice(H / KV);
+    if (choice == PrefillKernel::kPair && (H / KV) % 2 == 0)
+      return launch_prefill_pair<T, TO, D>(q, k, v, pos, out, n_q, t_kv, H, KV, scale, window,
+                                           kv_start, st);
+    if (choice != PrefillKernel::kSingle)
+      return launch_prefill_head<T, TO, D>(q, k, v, pos, out, n_q, t_kv, H, KV, scale, window,
+                                           kv_start, st);
+    const CUtensorMapDataType tdt = std::is_same<T, __nv_bfloat16>::value
+                                        ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap tq, tk, tv;
+    const uint64_t qdims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(H), static_cast<uint64_t>(n_q)};
+    const uint64_t qstr[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(H) * D * 2};
+    const uint64_t kdims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(KV), static_cast<uint64_t>(t_kv)};
+    const uint64_t kstr[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(KV) * D * 2};
+    const uint32_t box[3] = {64, 1, 128};
+    int rc = b2a_host::make_tmap(&tq, tdt, 3, const_cast<void*>(q), qdims, qstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = b2a_host::make_tmap(&tk, tdt, 3, const_cast<void*>(k), kdims, kstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = b2a_host::make_tmap(&tv, tdt, 3, const_cast<void*>(v), kdims, kstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    auto kern = prefill_kernel<T, TO, D>;
+    // >= 116 KB keeps one CTA per SM, so the 512-column TMEM allocation never
+    // waits on a co-resident CTA.
+    const int smem = Layout<D>::kSmem > 116 * 1024 ? Layout<D>::kSmem : 116 * 1024;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return b2a_host::cuda_fail(e, "cudaFuncSetAttribute(prefill)");
+    const int n_q_tiles = (n_q + kBM - 1) / kBM;
+    dim3 grid(n_q_tiles, H);
+    kern<<<grid, P::kThreads, smem, st>>>(tq, tk, tv, static_cast<const T*>(v), pos,
+                                          static_cast<TO*>(out), n_q, t_kv, H, H / KV, n_q_tiles,
+                                          scale * P::kLog2e, window, kv_start);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return b2a_host::cuda_fail(e, "prefill launch");
+    return B2A_OK;
+  }
 }
 
 template <typename T, int D>
@@ -579,7 +627,8 @@ int prefill_d(int D, int out_dtype, const void* q, const void* k, const void* v,
               cudaStream_t st) {
   if (D == 64) return prefill_out<T, 64>(out_dtype, q, k, v, pos, out, n_q, t_kv, H, KV, scale, window, kv_start, st);
   if (D == 128) return prefill_out<T, 128>(out_dtype, q, k, v, pos, out, n_q, t_kv, H, KV, scale, window, kv_start, st);
-  return fail(B2A_ERR_UNSUPPORTED, "prefill: head_dim %d (64 or 128)", D);
+  if (D == 256) return prefill_out<T, 256>(out_dtype, q, k, v, pos, out, n_q, t_kv, H, KV, scale, window, kv_start, st);
+  return fail(B2A_ERR_UNSUPPORTED, "prefill: 16-bit head_dim %d (64, 128 or 256)", D);
 }
 
 }  // namespace
@@ -598,9 +647,11 @@ extern "C" int b2a_prefill(const void* q, const void* k_cache, const void* v_cac
     return fail(B2A_ERR_ALIGN, "prefill: q, caches and out must be 16-byte aligned");
   if (n_q == 0) return B2A_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (in_dtype == B2A_F32)
+    return prefill_f32_dispatch(out_dtype, q, k_cache, v_cache, pos_dev, out, n_q, t_kv, H, KV, D, scale, window, kv_start, st);
   if (in_dtype == B2A_BF16)
     return prefill_d<__nv_bfloat16>(D, out_dtype, q, k_cache, v_cache, pos_dev, out, n_q, t_kv, H, KV, scale, window, kv_start, st);
   if (in_dtype == B2A_F16)
     return prefill_d<__half>(D, out_dtype, q, k_cache, v_cache, pos_dev, out, n_q, t_kv, H, KV, scale, window, kv_start, st);
-  return fail(B2A_ERR_DTYPE, "prefill: in_dtype %d (F16 or BF16)", in_dtype);
+  return fail(B2A_ERR_DTYPE, "prefill: in_dtype %d (F32, F16 or BF16)", in_dtype);
 }

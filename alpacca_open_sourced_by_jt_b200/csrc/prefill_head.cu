@@ -24,8 +24,11 @@
 //
 // 256 threads: warp 0 TMA producer, warp 1 TMEM owner + single-lane MMA
 // issuer, warps 2-3 idle, warps 4-7 softmax (thread = query row = TMEM lane).
-// TMEM (512 columns): S0/P0 [0,128), S1/P1 [128,256), O [256, 256+D).
-// SMEM (D=128): Q 32 KB, 6 K/V slots of 32 KB.
+// Key tiles hold BN keys: 128 for head_dim 64 and 128, 64 for head_dim 256,
+// where a 128-key K or V tile (64 KB) would leave room for only one ring slot.
+// TMEM (512 columns): S0/P0 [0,BN), S1/P1 [BN,2BN), O [2BN, 2BN+D) (for
+// D = 256: 64 + 64 + 256 columns).  SMEM: Q (128 x D), then a ring of K/V
+// slots of BN x D: 6 slots of 32 KB for D = 128, 5 of 32 KB for D = 256.
 //
 // Barrier phases use running counters; where one side may run two steps
 // ahead, two barriers alternate (index g & 1, phase g >> 1) so that every
@@ -63,16 +66,26 @@ using prefill::tc_wait_ld;
 using prefill::tc_wait_st;
 
 constexpr int kThreads = 256;
-constexpr int kSlots = 6;
 
+// Keys per K/V tile for a head_dim.
 template <int D>
+struct KeyTile {
+  static constexpr int kBN = D > 128 ? 64 : 128;
+};
+
+template <int D, int BN>
 struct Layout {
-  static constexpr int kBox = 128 * 128;         // 128 rows x 128 B
-  static constexpr int kTile = (D / 64) * kBox;  // Q, K or V tile (128 rows x D)
+  static constexpr int kSlots = D > 128 ? 5 : 6;
+  static constexpr int kBoxQ = 128 * 128;            // 128 query rows x 128 B
+  static constexpr int kBoxKV = BN * 128;            // BN key rows x 128 B
+  static constexpr int kTileQ = (D / 64) * kBoxQ;    // Q tile (128 rows x D)
+  static constexpr int kTileKV = (D / 64) * kBoxKV;  // K or V tile (BN rows x D)
   static constexpr int kQ = 0;
-  static constexpr int kRing = kTile;
-  static constexpr int kTotal = kRing + kSlots * kTile;
+  static constexpr int kRing = kTileQ;
+  static constexpr int kTotal = kRing + kSlots * kTileKV;
   static constexpr int kSmem = kTotal + 1024;
+  static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
+  static_assert(2 * BN + D <= 512, "S double buffer + O must fit in 512 TMEM columns");
 };
 
 struct Item {
@@ -81,6 +94,7 @@ struct Item {
 
 // The idx-th work item (heaviest q tiles first); every role computes the
 // same items from the same inputs.
+template <int BN>
 __device__ __forceinline__ Item make_item(int idx, const int* __restrict__ pos, int n_q,
                                           int t_kv, int H, int group, int n_q_tiles,
                                           int window, int kv_start) {
@@ -93,11 +107,11 @@ __device__ __forceinline__ Item make_item(int idx, const int* __restrict__ pos, 
   const long long pf = pos[it.row0];
   const long long pl = pos[it.row0 + it.nrows - 1];
   const long long hi = min(pl - kv_start + 1, static_cast<long long>(t_kv));
-  it.jend = hi <= 0 ? 0 : static_cast<int>((hi + kBN - 1) / kBN);
+  it.jend = hi <= 0 ? 0 : static_cast<int>((hi + BN - 1) / BN);
   it.j0 = 0;
   if (window > 0) {
     const long long lo = pf - window + 1 - kv_start;
-    if (lo > 0) it.j0 = static_cast<int>(min(lo / kBN, static_cast<long long>(it.jend)));
+    if (lo > 0) it.j0 = static_cast<int>(min(lo / BN, static_cast<long long>(it.jend)));
   }
   return it;
 }
@@ -109,10 +123,12 @@ __device__ __forceinline__ int item_index(int k, int c, int G) {
 template <typename T, typename TO, int D>
 __global__ void __launch_bounds__(kThreads, 1) prefill_head_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-    const __grid_constant__ CUtensorMap tmV, const int* __restrict__ pos, TO* __restrict__ out,
-    int n_q, int t_kv, int H, int group, int n_q_tiles, int n_items, float sscale, int window,
-    int kv_start) {
-  using L = Layout<D>;
+    const __grid_constant__ CUtensorMap tmV, const T* __restrict__ vraw,
+    const int* __restrict__ pos, TO* __restrict__ out, int n_q, int t_kv, int H, int group,
+    int n_q_tiles, int n_items, float sscale, int window, int kv_start) {
+  constexpr int BN = KeyTile<D>::kBN;
+  using L = Layout<D, BN>;
+  constexpr int kSlots = L::kSlots;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_qf, bar_qe;
   __shared__ __align__(8) uint64_t bar_full[kSlots], bar_empty[kSlots];
@@ -161,13 +177,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_head_kernel(
       for (int k = 0; ok; ++k) {
         const int idx = item_index(k, c, G);
         if (idx >= n_items) break;
-        const Item it = make_item(idx, pos, n_q, t_kv, H, group, n_q_tiles, window, kv_start);
+        const Item it = make_item<BN>(idx, pos, n_q, t_kv, H, group, n_q_tiles, window, kv_start);
         if (it.jend - it.j0 <= 0) continue;
         if (qcnt > 0 && !mbar_wait(&bar_qe, (qcnt - 1) & 1, 0x21000 | k)) break;
-        mbar_arrive_expect_tx(&bar_qf, L::kTile);
+        mbar_arrive_expect_tx(&bar_qf, L::kTileQ);
 #pragma unroll
         for (int b = 0; b < D / 64; ++b)
-          tma_load_3d(smem + L::kQ + b * L::kBox, &tmQ, &bar_qf, b * 64, it.h, it.row0);
+          tma_load_3d(smem + L::kQ + b * L::kBoxQ, &tmQ, &bar_qf, b * 64, it.h, it.row0);
         ++qcnt;
         for (int j = it.j0; ok && j < it.jend; ++j) {
 #pragma unroll
@@ -178,12 +194,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_head_kernel(
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&bar_full[slot], L::kTile);
-            uint8_t* dst = smem + L::kRing + slot * L::kTile;
+            mbar_arrive_expect_tx(&bar_full[slot], L::kTileKV);
+            uint8_t* dst = smem + L::kRing + slot * L::kTileKV;
 #pragma unroll
             for (int b = 0; b < D / 64; ++b)
-              tma_load_3d(dst + b * L::kBox, kv ? &tmV : &tmK, &bar_full[slot], b * 64, it.kvh,
-                          j * kBN);
+              tma_load_3d(dst + b * L::kBoxKV, kv ? &tmV : &tmK, &bar_full[slot], b * 64, it.kvh,
+                          j * BN);
             ++seq;
           }
         }
@@ -192,33 +208,34 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_head_kernel(
   } else if (warp == 1) {
     // ------------------------------ MMA issuer -----------------------------
     if (lane == 0) {
-      constexpr uint32_t idesc_qk = make_idesc<T>(kBM, kBN, false, false);
+      constexpr uint32_t idesc_qk = make_idesc<T>(kBM, BN, false, false);
       constexpr uint32_t idesc_pv = make_idesc<T>(kBM, D, false, true);
       // Descriptors precomputed once: the start address sits in the low 14
       // bits (address >> 4), so a byte offset becomes an add of (off >> 4).
       const uint64_t dQ = sw128_desc(smem_u32(smem + L::kQ), 16, 1024);
       const uint64_t dK0 = sw128_desc(smem_u32(smem + L::kRing), 16, 1024);
-      const uint64_t dV0 = sw128_desc(smem_u32(smem + L::kRing), L::kBox, 1024);
-      constexpr uint64_t kSlotStep = L::kTile >> 4;
+      const uint64_t dV0 = sw128_desc(smem_u32(smem + L::kRing), L::kBoxKV, 1024);
+      constexpr uint64_t kSlotStep = L::kTileKV >> 4;
       uint32_t seq = 0, qcnt = 0, pcnt = 0, pvg = 0;
       bool ok = true;
       auto qk = [&](int jj, uint32_t kslot) {
         const uint64_t dk = dK0 + kslot * kSlotStep;
-        const uint32_t d_tm = tmem + (jj & 1) * kBN;
+        const uint32_t d_tm = tmem + (jj & 1) * BN;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t off = (((kk >> 2) * L::kBox) + (kk & 3) * 32) >> 4;
-          tc_mma(d_tm, dQ + off, dk + off, idesc_qk, kk > 0);
+          const uint64_t qoff = (((kk >> 2) * L::kBoxQ) + (kk & 3) * 32) >> 4;
+          const uint64_t koff = (((kk >> 2) * L::kBoxKV) + (kk & 3) * 32) >> 4;
+          tc_mma(d_tm, dQ + qoff, dk + koff, idesc_qk, kk > 0);
         }
         tc_commit(&bar_sf[jj & 1]);
       };
       auto pv = [&](int jj, uint32_t vslot) {
         const uint64_t dv = dV0 + vslot * kSlotStep;
-        const uint32_t tp = tmem + (jj & 1) * kBN;  // P(jj): 16 keys per 8 columns
+        const uint32_t tp = tmem + (jj & 1) * BN;  // P(jj): 16 keys per 8 columns
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
+        for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t voff = (kk * 16 * 128) >> 4;
-          tc_mma_ts(tmem + 2 * kBN, tp + kk * 8, dv + voff, idesc_pv, (jj > 0 || kk > 0));
+          tc_mma_ts(tmem + 2 * BN, tp + kk * 8, dv + voff, idesc_pv, (jj > 0 || kk > 0));
         }
         tc_commit(&bar_pv[pvg & 1]);
         ++pvg;
@@ -226,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_head_kernel(
       for (int k = 0; ok; ++k) {
         const int idx = item_index(k, c, G);
         if (idx >= n_items) break;
-        const Item it = make_item(idx, pos, n_q, t_kv, H, group, n_q_tiles, window, kv_start);
+        const Item it = make_item<BN>(idx, pos, n_q, t_kv, H, group, n_q_tiles, window, kv_start);
         const int n = it.jend - it.j0;
         if (n <= 0) continue;
         if (!mbar_wait(&bar_qf, qcnt & 1, 0x23000 | k)) break;
@@ -266,13 +283,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_head_kernel(
     // ------------------------------ softmax ----------------------------------
     const int r = (warp & 3) * 32 + lane;  // query row within the tile == TMEM lane
     const uint32_t tl = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    const uint32_t o_col = 2 * kBN;
+    const uint32_t o_col = 2 * BN;
     uint32_t scnt0 = 0, scnt1 = 0, pfg = 0, pvbase = 0;
     bool ok = true;
     for (int k = 0; ok; ++k) {
       const int idx = item_index(k, c, G);
       if (idx >= n_items) break;
-      const Item it = make_item(idx, pos, n_q, t_kv, H, group, n_q_tiles, window, kv_start);
+      const Item it = make_item<BN>(idx, pos, n_q, t_kv, H, group, n_q_tiles, window, kv_start);
       const int n = it.jend - it.j0;
       const int row = it.row0 + r;
       const bool valid_row = r < it.nrows;
@@ -281,16 +298,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_head_kernel(
       if (valid_row && n > 0) {
         const long long last = min(my_pos, static_cast<long long>(kv_start) + t_kv - 1) - kv_start;
         const long long first = window > 0 ? my_pos - window + 1 - kv_start : 0;
-        if ((last >= 0 && last / kBN >= it.jend) || (first > 0 && first / kBN < it.j0))
+        if ((last >= 0 && last / BN >= it.jend) || (first > 0 && first / BN < it.j0))
           set_dev_error(B2A_ERR_POSITION, row);
       }
       if (n <= 0) {
-        float z[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) z[e] = 0.f;
-        if (valid_row)
-#pragma unroll
-          for (int cc = 0; cc < D / 32; ++cc) store_row32<TO>(orow + cc * 32, z, 1.f);
+        // no key visible to any row of the tile
+        prefill::store_mean_v_rows<T, TO>(valid_row, orow, vraw, t_kv, H / group, it.kvh, D);
         continue;
       }
       float m = -INFINITY, l = 0.f;
@@ -302,27 +315,27 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_head_kernel(
         if (!ok) break;
         ++sc;
         tc_fence_after();
-        float s[kBN];
+        float s[BN];
 #pragma unroll
-        for (int q32 = 0; q32 < kBN / 32; ++q32)
-          tc_ld32(tl + sb * kBN + q32 * 32, s + q32 * 32);
+        for (int q32 = 0; q32 < BN / 32; ++q32)
+          tc_ld32(tl + sb * BN + q32 * 32, s + q32 * 32);
         tc_wait_ld();
 
-        const long long kv0 = static_cast<long long>(kv_start) + static_cast<long long>(j) * kBN;
-        const int hi = valid_row ? static_cast<int>(min(my_pos - kv0, static_cast<long long>(min(kBN, t_kv - j * kBN) - 1)))
+        const long long kv0 = static_cast<long long>(kv_start) + static_cast<long long>(j) * BN;
+        const int hi = valid_row ? static_cast<int>(min(my_pos - kv0, static_cast<long long>(min(BN, t_kv - j * BN) - 1)))
                                  : -1;
         const int lo = (window > 0 && valid_row)
                            ? static_cast<int>(max(my_pos - window + 1 - kv0, -1ll))
                            : -1;
         // branch-free mask select (a short-circuit test compiles to a branch
         // per element); four partial maxima keep the FMNMX chain short
-        if (!(hi >= kBN - 1 && lo <= 0)) {
+        if (!(hi >= BN - 1 && lo <= 0)) {
 #pragma unroll
-          for (int cc = 0; cc < kBN; ++cc) s[cc] = ((cc <= hi) & (cc >= lo)) ? s[cc] : -INFINITY;
+          for (int cc = 0; cc < BN; ++cc) s[cc] = ((cc <= hi) & (cc >= lo)) ? s[cc] : -INFINITY;
         }
         float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;
 #pragma unroll
-        for (int cc = 0; cc < kBN; cc += 4) {
+        for (int cc = 0; cc < BN; cc += 4) {
           mxa = fmaxf(mxa, s[cc]);
           mxb = fmaxf(mxb, s[cc + 1]);
           mxc = fmaxf(mxc, s[cc + 2]);
@@ -336,11 +349,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_head_kernel(
           m = mnew;
         }
         const float mref = (m == -INFINITY) ? 0.f : m;
-        // P(jj) as 16-bit pairs over the first 64 columns of S buffer jj % 2
+        // P(jj) as 16-bit pairs over the first BN/2 columns of S buffer jj % 2
         // (the whole score row is already in registers); 32 keys per store
         float suma = 0.f, sumb = 0.f;
 #pragma unroll
-        for (int qtr = 0; qtr < 4; ++qtr) {
+        for (int qtr = 0; qtr < BN / 32; ++qtr) {
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
@@ -349,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_head_kernel(
             if (e & 1) sumb += p0 + p1; else suma += p0 + p1;
             pk[e] = Pack2<T>::run(p0, p1);
           }
-          tc_st16(tl + sb * kBN + qtr * 16, pk);
+          tc_st16(tl + sb * BN + qtr * 16, pk);
         }
         tc_wait_st();
         l = l * alpha + (suma + sumb);
@@ -391,11 +404,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_head_kernel(
         float o[32];
         tc_ld32(tl + o_col + cc * 32, o);
         tc_wait_ld();
-        if (valid_row) store_row32<TO>(orow + cc * 32, o, inv);
+        if (valid_row && l > 0.f) store_row32<TO>(orow + cc * 32, o, inv);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_oe);
+      prefill::store_mean_v_rows<T, TO>(valid_row && !(l > 0.f), orow, vraw, t_kv, H / group,
+                                        it.kvh, D);
     }
   }
   // ------------------------------ teardown -----------------------------------
@@ -417,25 +432,41 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_head_kernel(
 namespace {
 
 template <typename T, typename TO, int D>
-int launch_prefill_head(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                        const int* pos, void* out, int n_q, int t_kv, int H, int KV, float scale,
-                        int window, int kv_start, cudaStream_t st) {
+int launch_prefill_head(const void* q, const void* k, const void* v, const int* pos, void* out,
+                        int n_q, int t_kv, int H, int KV, float scale, int window, int kv_start,
+                        cudaStream_t st) {
   namespace PH = b2a::prefill_head;
+  constexpr int BN = PH::KeyTile<D>::kBN;
+  using L = PH::Layout<D, BN>;
   auto kern = PH::prefill_head_kernel<T, TO, D>;
+  const CUtensorMapDataType tdt = std::is_same<T, __nv_bfloat16>::value
+                                      ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tq, tk, tv;
+  const uint64_t qdims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(H), static_cast<uint64_t>(n_q)};
+  const uint64_t qstr[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(H) * D * 2};
+  const uint64_t kdims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(KV), static_cast<uint64_t>(t_kv)};
+  const uint64_t kstr[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(KV) * D * 2};
+  const uint32_t qbox[3] = {64, 1, 128};
+  const uint32_t kvbox[3] = {64, 1, static_cast<uint32_t>(BN)};
+  int rc = b2a_host::make_tmap(&tq, tdt, 3, const_cast<void*>(q), qdims, qstr, qbox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = b2a_host::make_tmap(&tk, tdt, 3, const_cast<void*>(k), kdims, kstr, kvbox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = b2a_host::make_tmap(&tv, tdt, 3, const_cast<void*>(v), kdims, kstr, kvbox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
   // >= 120 KB keeps one CTA per SM: a second resident CTA would wait in its
   // 512-column TMEM allocation while another SM idles.
-  const int smem = PH::Layout<D>::kSmem > 120 * 1024 ? PH::Layout<D>::kSmem : 120 * 1024;
+  const int smem = L::kSmem > 120 * 1024 ? L::kSmem : 120 * 1024;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "cudaFuncSetAttribute(prefill_head)");
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = b2a_host::sm_count();
   const int n_q_tiles = (n_q + b2a::prefill::kBM - 1) / b2a::prefill::kBM;
   const int n_items = n_q_tiles * H;
   const int grid = n_items < sms ? n_items : sms;
-  kern<<<grid, PH::kThreads, smem, st>>>(tq, tk, tv, pos, static_cast<TO*>(out), n_q, t_kv, H,
-                                         H / KV, n_q_tiles, n_items,
-                                         scale * b2a::prefill::kLog2e, window, kv_start);
+  kern<<<grid, PH::kThreads, smem, st>>>(tq, tk, tv, static_cast<const T*>(v), pos,
+                                         static_cast<TO*>(out), n_q, t_kv, H, H / KV, n_q_tiles,
+                                         n_items, scale * b2a::prefill::kLog2e, window, kv_start);
   e = cudaGetLastError();
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "prefill_head launch");
   return B2A_OK;

@@ -130,9 +130,9 @@ __device__ __forceinline__ int item_index(int k, int c, int G) {
 template <typename T, typename TO, int D>
 __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-    const __grid_constant__ CUtensorMap tmV, const int* __restrict__ pos, TO* __restrict__ out,
-    int n_q, int t_kv, int H, int group, int n_q_tiles, int n_items, float sscale, int window,
-    int kv_start) {
+    const __grid_constant__ CUtensorMap tmV, const T* __restrict__ vraw,
+    const int* __restrict__ pos, TO* __restrict__ out, int n_q, int t_kv, int H, int group,
+    int n_q_tiles, int n_items, float sscale, int window, int kv_start) {
   using L = Layout<D>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_qf, bar_qe;
@@ -322,12 +322,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
           set_dev_error(B2A_ERR_POSITION, row);
       }
       if (n <= 0) {
-        float z[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) z[e] = 0.f;
-        if (valid_row)
-#pragma unroll
-          for (int cc = 0; cc < D / 32; ++cc) store_row32<TO>(orow + cc * 32, z, 1.f);
+        // no key visible to any row of the tile
+        prefill::store_mean_v_rows<T, TO>(valid_row, orow, vraw, t_kv, H / group, it.kvh, D);
         continue;
       }
       float m = -INFINITY, l = 0.f;
@@ -431,11 +427,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
         float o[32];
         tc_ld32(tl + o_col + cc * 32, o);
         tc_wait_ld();
-        if (valid_row) store_row32<TO>(orow + cc * 32, o, inv);
+        if (valid_row && l > 0.f) store_row32<TO>(orow + cc * 32, o, inv);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_oe[t]);
+      prefill::store_mean_v_rows<T, TO>(valid_row && !(l > 0.f), orow, vraw, t_kv, H / group,
+                                        it.kvh, D);
     }
   }
   // ------------------------------ teardown -----------------------------------
@@ -489,13 +487,12 @@ int launch_prefill_pair(const void* q, const void* k, const void* v, const int* 
   const int smem = P2::Layout<D>::kSmem > 120 * 1024 ? P2::Layout<D>::kSmem : 120 * 1024;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "cudaFuncSetAttribute(prefill_pair)");
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = b2a_host::sm_count();
   const int n_q_tiles = (n_q + b2a::prefill::kBM - 1) / b2a::prefill::kBM;
   const int n_items = n_q_tiles * (H / 2);
   const int grid = n_items < sms ? n_items : sms;
-  kern<<<grid, P2::kThreads, smem, st>>>(tq, tk, tv, pos, static_cast<TO*>(out), n_q, t_kv, H,
+  kern<<<grid, P2::kThreads, smem, st>>>(tq, tk, tv, static_cast<const T*>(v), pos,
+                                         static_cast<TO*>(out), n_q, t_kv, H,
                                          H / KV, n_q_tiles, n_items,
                                          scale * b2a::prefill::kLog2e, window, kv_start);
   e = cudaGetLastError();

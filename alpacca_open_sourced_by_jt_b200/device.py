@@ -154,16 +154,22 @@ def lse_combine(o_parts: torch.Tensor, lse_parts: torch.Tensor, *, out=None, lse
 def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, positions: torch.Tensor, *,
             scale: float | None = None, window: int = 0, kv_start: int = 0,
             out_dtype: torch.dtype | None = None, out=None, stream=None) -> torch.Tensor:
-    """Causal flash prefill on tcgen05.
+    """Causal flash prefill.
 
-    q (T, H, D) f16/bf16; k, v (t_kv, KV, D) same dtype (the cache rows
-    kv_start..kv_start+t_kv-1); positions (T,) int32 absolute positions.
-    Returns (T, H, D) in out_dtype (default q.dtype)."""
+    q (T, H, D); k, v (t_kv, KV, D) (the cache rows kv_start..kv_start+t_kv-1),
+    all of one dtype; positions (T,) int32 absolute positions.  f16/bf16
+    inputs run the tcgen05 tensor-core kernels (D in {64, 128, 256}, fp32
+    accumulation); f32 inputs run the fp32 CUDA-core kernel (D a multiple of
+    4 up to 256), which keeps the reference's fp32 precision.  A query row
+    with no visible key gets the mean of the t_kv value rows, as the
+    reference's NumPy path does.  Returns (T, H, D) in out_dtype (default
+    q.dtype)."""
     for n_, t_ in (("q", q), ("k", k), ("v", v), ("positions", positions)):
         _cuda_contig(n_, t_)
     _need(q.dim() == 3 and k.dim() == 3 and k.shape == v.shape, "q (T,H,D), k/v (t_kv,KV,D)")
-    _need(q.dtype == k.dtype == v.dtype and q.dtype in (torch.float16, torch.bfloat16),
-          "q/k/v must share dtype f16 or bf16")
+    _need(q.dtype == k.dtype == v.dtype and q.dtype in (torch.float32, torch.float16,
+                                                         torch.bfloat16),
+          "q/k/v must share dtype f32, f16 or bf16")
     T, H, D = q.shape
     t_kv, KV, Dk = k.shape
     _need(Dk == D, "head_dim mismatch")

@@ -40,7 +40,8 @@ def _attention_np(self, q, K, V, group: int, inv_sqrt: float):
 def _attention_batch_np(self, q, K, V, positions, group: int, inv_sqrt: float):
     out = _cuda.attention_batch(q, K, V, positions, group, inv_sqrt)
     if out is None:
-        raise ValueError(f"B200 prefill does not serve head_dim {self.hp.head_dim}")
+        raise ValueError(f"B200 prefill does not serve head_dim {self.hp.head_dim} "
+                         "(a multiple of 4 up to 256); no CPU fallback is installed")
     return out
 
 
@@ -48,7 +49,8 @@ def _attention_batch_window_np(self, q, K, V, positions, group: int, inv_sqrt: f
                                window: int = 0, kv_start: int = 0):
     out = _cuda.attention_batch(q, K, V, positions, group, inv_sqrt, window, kv_start)
     if out is None:
-        raise ValueError(f"B200 prefill does not serve head_dim {self.hp.head_dim}")
+        raise ValueError(f"B200 prefill does not serve head_dim {self.hp.head_dim} "
+                         "(a multiple of 4 up to 256); no CPU fallback is installed")
     return out
 
 

@@ -152,14 +152,23 @@ int b2a_lse_combine(const float* o_parts, long long o_part_stride, const float* 
  * cuda.attention_batch / _attention_batch_gqa (alpaccaroo/cuda.py:424-578,
  * 1186-1242) and qwen35_full_attention_prefill (qwen35_kernels.py:395-411).
  *
- *   q        in_dtype [T][H][D]   rotated queries (F16 or BF16)
+ *   q        in_dtype [T][H][D]   rotated queries (F32, F16 or BF16)
  *   k_cache  in_dtype [t_kv][KV][D] rows kv_start .. kv_start+t_kv-1
  *   v_cache  same
  *   pos_dev  int32 [T]            absolute position of each query token
  *   out      out_dtype [T][H][D]  (F32, F16 or BF16)
  * Key s (absolute position kv_start+s) is visible to query t iff
  * kv_start+s <= pos[t] and (window <= 0 or kv_start+s > pos[t]-window).
- * A query row with no visible key gets 0.  D must be 64 or 128. */
+ * A query row with no visible key gets the mean of the t_kv value rows of
+ * its KV head, the NumPy path's result (its -1e30 mask weighs every key
+ * equally).
+ *   F16 / BF16 inputs: tcgen05 tensor cores, fp32 accumulation, P rounded
+ *     to the input type; D in {64, 128, 256}; positions non-decreasing
+ *     within each 128-token tile (a row outside its tile's key range
+ *     records B2A_ERR_POSITION).
+ *   F32 inputs: fp32 products and accumulation on the CUDA cores (the
+ *     reference's precision); D a multiple of 4, at most 256; positions in
+ *     any order. */
 int b2a_prefill(const void* q, const void* k_cache, const void* v_cache, const int* pos_dev,
                 void* out, int T, int t_kv, int H, int KV, int D, int in_dtype, int out_dtype,
                 float scale, int window, int kv_start, void* stream);

@@ -74,6 +74,57 @@ def prefill_window():
                 sha256=_digest(q, k, v, positions))
 
 
+def prefill_qwen35_d256():
+    """Qwen35 full-attention prefill at its key_length 256: 12 tokens after a
+    13-token prefix, 4 q / 2 KV heads, fp32 N(0,1)."""
+    rng = np.random.default_rng(41)
+    q = rng.standard_normal((12, 4, 256), dtype=np.float32)
+    k = rng.standard_normal((25, 2, 256), dtype=np.float32)
+    v = rng.standard_normal((25, 2, 256), dtype=np.float32)
+    return dict(q=q, k=k, v=v, prefix=13, sha256=_digest(q, k, v))
+
+
+def prefill_gemma3_window_d256():
+    """gemma3-style sliding-window prefill at head_dim 256 (the geometry the
+    reference's GPU tier declines): 4 q / 1 KV head, window 24, kv_start 7,
+    24 queries at positions 40..63 over the 57 cached rows 7..63."""
+    H, KV, D, t = 4, 1, 256, 24
+    rng = np.random.default_rng(42)
+    q = rng.standard_normal((t, H, D), dtype=np.float32)
+    k = rng.standard_normal((57, KV, D), dtype=np.float32)
+    v = rng.standard_normal((57, KV, D), dtype=np.float32)
+    positions = np.arange(40, 40 + t, dtype=np.int32)
+    return dict(H=H, KV=KV, D=D, window=24, kv_start=7, q=q, k=k, v=v, positions=positions,
+                sha256=_digest(q, k, v, positions))
+
+
+def prefill_empty_rows():
+    """Rows with no visible key: kv_start 20 with queries at positions
+    10..29, so rows 0..9 precede every cached key (the NumPy path gives them
+    the mean of all value rows), plus a window of 4.  4 q / 2 KV heads, 64."""
+    H, KV, D, t = 4, 2, 64, 20
+    rng = np.random.default_rng(43)
+    q = rng.standard_normal((t, H, D), dtype=np.float32)
+    k = rng.standard_normal((10, KV, D), dtype=np.float32)
+    v = rng.standard_normal((10, KV, D), dtype=np.float32)
+    positions = np.arange(10, 10 + t, dtype=np.int32)
+    return dict(H=H, KV=KV, D=D, window=4, kv_start=20, q=q, k=k, v=v, positions=positions,
+                sha256=_digest(q, k, v, positions))
+
+
+def prefill_large_magnitude():
+    """fp32 values far outside fp16's range: q ~ N(0, 30^2) (peaked softmax
+    rows), K ~ N(0,1), V ~ N(0, 1e5^2); causal over 40 keys with a 24-row
+    prefix, 4 q / 2 KV heads, head_dim 128."""
+    rng = np.random.default_rng(44)
+    q = (30.0 * rng.standard_normal((16, 4, 128))).astype(np.float32)
+    k = rng.standard_normal((40, 2, 128), dtype=np.float32)
+    v = (1e5 * rng.standard_normal((40, 2, 128))).astype(np.float32)
+    positions = np.arange(24, 40, dtype=np.int32)
+    return dict(H=4, KV=2, D=128, q=q, k=k, v=v, positions=positions,
+                sha256=_digest(q, k, v, positions))
+
+
 def qwen35_decode():
     """Qwen35 full-attention decode: 8 q / 2 KV heads, head_dim 64, 40 keys."""
     rng = np.random.default_rng(31)

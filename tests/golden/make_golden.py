@@ -86,6 +86,33 @@ def make_prefill(model_mod):
                         out=out, window_input_sha256=w["sha256"], out_window=outw)
 
 
+def make_prefill_more(model_mod, qk_mod):
+    """Prefill geometries beyond the first fixture: Qwen35 at head_dim 256
+    with a prefix (qwen35_kernels.py:395-411), gemma3's window variant at
+    head_dim 256 (model.py:1567-1592), rows with no visible key, and fp32
+    values outside fp16's range (model.py:1254-1272)."""
+    c = cases.prefill_qwen35_d256()
+    q35 = qk_mod.qwen35_full_attention_prefill(c["q"], c["k"], c["v"], c["prefix"])
+    w = cases.prefill_gemma3_window_d256()
+    m = _llama_model(model_mod, 128, w["H"], w["KV"], w["D"], w["D"], 10000.0, "norm")
+    win = m._attention_batch_window_np(w["q"], w["k"], w["v"], w["positions"],
+                                       w["H"] // w["KV"], 1.0 / np.sqrt(w["D"]),
+                                       w["window"], w["kv_start"])
+    e = cases.prefill_empty_rows()
+    m = _llama_model(model_mod, 64, e["H"], e["KV"], e["D"], e["D"], 10000.0, "norm")
+    empty = m._attention_batch_window_np(e["q"], e["k"], e["v"], e["positions"],
+                                         e["H"] // e["KV"], 1.0 / np.sqrt(e["D"]),
+                                         e["window"], e["kv_start"])
+    g = cases.prefill_large_magnitude()
+    m = _llama_model(model_mod, 64, g["H"], g["KV"], g["D"], g["D"], 10000.0, "norm")
+    big = m._attention_batch_np(g["q"], g["k"], g["v"], g["positions"], g["H"] // g["KV"],
+                                1.0 / np.sqrt(g["D"]))
+    np.savez_compressed(
+        os.path.join(HERE, "prefill_more.npz"), qwen35_d256_sha256=c["sha256"],
+        qwen35_d256=q35, window_d256_sha256=w["sha256"], window_d256=win,
+        empty_rows_sha256=e["sha256"], empty_rows=empty, large_sha256=g["sha256"], large=big)
+
+
 def make_qwen35(qk_mod, ops_mod):
     c = cases.qwen35_decode()
     out = qk_mod.qwen35_full_attention_decode(c["q"], c["k"], c["v"])
@@ -230,6 +257,7 @@ def main():
     make_decode_config1(model_mod)
     make_rope_neox(model_mod)
     make_prefill(model_mod)
+    make_prefill_more(model_mod, qk_mod)
     make_qwen35(qk_mod, ops_mod)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):

@@ -85,10 +85,18 @@ def test_prefill_rejects_bad_arguments(lib):
                            None) == _lib.ERR_ARG
     assert lib.b2a_prefill(p, p, p, p, p, 8, 8, 5, 2, 64, _lib.BF16, _lib.F32, 0.1, 0, 0,
                            None) == _lib.ERR_SHAPE
-    assert lib.b2a_prefill(p, p, p, p, p, 8, 8, 4, 2, 64, _lib.F32, _lib.F32, 0.1, 0, 0,
+    assert lib.b2a_prefill(p, p, p, p, p, 8, 8, 4, 2, 64, 7, _lib.F32, 0.1, 0, 0,
                            None) == _lib.ERR_DTYPE
+    # 16-bit inputs: head_dim 64, 128 or 256 (tensor cores); f32 inputs: a
+    # multiple of 4 up to 256 (fp32 kernel)
     assert lib.b2a_prefill(p, p, p, p, p, 8, 8, 4, 2, 96, _lib.BF16, _lib.F32, 0.1, 0, 0,
                            None) == _lib.ERR_UNSUPPORTED
+    assert lib.b2a_prefill(p, p, p, p, p, 8, 8, 4, 2, 6, _lib.F32, _lib.F32, 0.1, 0, 0,
+                           None) == _lib.ERR_UNSUPPORTED
+    assert lib.b2a_prefill(p, p, p, p, p, 8, 8, 4, 2, 260, _lib.F32, _lib.F32, 0.1, 0, 0,
+                           None) == _lib.ERR_UNSUPPORTED
+    assert lib.b2a_prefill(p, p, p, p, p, 8, 8, 4, 2, 64, _lib.F32, 9, 0.1, 0, 0,
+                           None) == _lib.ERR_DTYPE
     assert lib.b2a_prefill(p + 2, p, p, p, p, 8, 8, 4, 2, 64, _lib.BF16, _lib.F32, 0.1, 0, 0,
                            None) == _lib.ERR_ALIGN
     # zero query tokens is a successful no-op

@@ -68,6 +68,36 @@ def test_prefill_matches_reference(golden):
     assert rel_err(outw, g["out_window"]) < 1e-5
 
 
+def test_prefill_more_matches_reference(golden):
+    """Head_dim 256 (Qwen35 with a prefix, gemma3's window), rows with no
+    visible key, fp32 values outside fp16's range."""
+    g = golden("prefill_more.npz")
+    c = cases.prefill_qwen35_d256()
+    assert c["sha256"] == str(g["qwen35_d256_sha256"])
+    assert rel_err(oracle.qwen35_full_attention_prefill(c["q"], c["k"], c["v"], c["prefix"]),
+                   g["qwen35_d256"]) < 1e-5
+    for name, case in (("window_d256", cases.prefill_gemma3_window_d256()),
+                       ("empty_rows", cases.prefill_empty_rows())):
+        assert case["sha256"] == str(g[name + "_sha256"])
+        out = oracle.attention_batch(case["q"], case["k"], case["v"], case["positions"],
+                                     case["H"] // case["KV"], 1.0 / math.sqrt(case["D"]),
+                                     case["window"], case["kv_start"])
+        assert rel_err(out, g[name]) < 1e-5
+    # rows 0..9 of the empty-row case see no key: the reference gives them
+    # the mean of all value rows (its -1e30 mask weighs every key equally)
+    e = cases.prefill_empty_rows()
+    mean_v = e["v"].mean(axis=0)  # (KV, D)
+    got = g["empty_rows"].reshape(20, e["H"], e["D"])[:10]
+    want = np.repeat(mean_v, e["H"] // e["KV"], axis=0)[None]
+    assert np.abs(got - want).max() < 1e-6
+    b = cases.prefill_large_magnitude()
+    assert b["sha256"] == str(g["large_sha256"])
+    out = oracle.attention_batch(b["q"], b["k"], b["v"], b["positions"], b["H"] // b["KV"],
+                                 1.0 / math.sqrt(b["D"]))
+    assert rel_err(out, g["large"]) < 1e-5
+    assert np.abs(g["large"]).max() > 6.5e4  # beyond fp16's largest finite value
+
+
 def test_qwen35_paths_match_reference(golden):
     g = golden("qwen35.npz")
     c = cases.qwen35_decode()
