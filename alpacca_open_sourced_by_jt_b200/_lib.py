@@ -58,6 +58,14 @@ SIGNATURES = [
     ("b2a_decode_noalloc", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                    c_int, c_int, c_int, c_int, c_int, c_longlong, c_int,
                                    c_float, c_int, c_int, c_void_p]),
+    ("b2a_shard_exchange_bytes", c_size_t, [c_int, c_int, c_int, c_int]),
+    ("b2a_decode_sharded", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                   c_void_p, c_size_t, c_int, c_int, c_int, c_int, c_int,
+                                   c_longlong, c_int, c_float, c_int, c_int, c_void_p, c_int,
+                                   c_int, c_void_p]),
+    ("b2a_ipc_handle", c_int, [c_void_p, c_void_p, POINTER(c_longlong)]),
+    ("b2a_ipc_open", c_int, [c_void_p, c_longlong, POINTER(c_void_p), POINTER(c_void_p)]),
+    ("b2a_ipc_close", c_int, [c_void_p]),
     ("b2a_lse_combine", c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_int, c_int, c_int,
                                 c_void_p, c_void_p, c_void_p]),
     ("b2a_prefill", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,

@@ -692,11 +692,19 @@ size_t b2a_decode_workspace_bytes(int B, int H, int D, int max_len, int split_ro
   return part_o_bytes(B, H, D, ns) + round_up(static_cast<size_t>(B) * H * ns * 2 * sizeof(float), 256);
 }
 
-int b2a_decode(const float* q, const void* k_cache, const void* v_cache, const int* lens_dev,
-               float* out, float* lse_out, void* workspace, size_t workspace_bytes, int B, int H,
-               int KV, int D, int n_ctx, long long seq_stride, int kv_dtype, float scale,
-               int max_len, int split_rows, void* stream) {
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+}  // extern "C"
+
+namespace {
+
+// Argument checks and the split kernel of a decode call (everything but the
+// combine): the partials land in the workspace, part_o then part_ml.  On
+// success *ns_out holds the number of splits and *split_rows_io the split.
+int decode_split_phase(const float* q, const void* k_cache, const void* v_cache,
+                       const int* lens_dev, const void* out, void* workspace,
+                       size_t workspace_bytes, int B, int H, int KV, int D, int n_ctx,
+                       long long seq_stride, int kv_dtype, float scale, int max_len,
+                       int* split_rows_io, int* ns_out, float** part_o_out, float** part_ml_out,
+                       cudaStream_t st) {
   if (!q || !k_cache || !v_cache || !lens_dev || !out)
     return fail(B2A_ERR_ARG, "decode: null pointer argument");
   if (B <= 0 || H <= 0 || KV <= 0 || D <= 0 || n_ctx <= 0 || max_len < 0)
@@ -713,6 +721,7 @@ int b2a_decode(const float* q, const void* k_cache, const void* v_cache, const i
   const int es = b2a_host::elem_size(kv_dtype);
   if (es == 0) return fail(B2A_ERR_DTYPE, "decode: kv_dtype %d", kv_dtype);
   if (!(scale > 0.f) || !isfinite(scale)) return fail(B2A_ERR_ARG, "decode: scale must be positive");
+  int split_rows = *split_rows_io;
   if (split_rows <= 0) split_rows = b2a_decode_split_rows(B, KV, max_len, kv_dtype);
   if (split_rows % kRows != 0)
     return fail(B2A_ERR_ARG, "decode: split_rows %d is not a multiple of %d", split_rows, kRows);
@@ -770,6 +779,29 @@ int b2a_decode(const float* q, const void* k_cache, const void* v_cache, const i
   }
   const int smem = ns * static_cast<int>(sizeof(float));
   if (smem > 48 * 1024) return fail(B2A_ERR_UNSUPPORTED, "decode: %d splits exceed the combine limit", ns);
+  *split_rows_io = split_rows;
+  *ns_out = ns;
+  *part_o_out = part_o;
+  *part_ml_out = part_ml;
+  return B2A_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b2a_decode(const float* q, const void* k_cache, const void* v_cache, const int* lens_dev,
+               float* out, float* lse_out, void* workspace, size_t workspace_bytes, int B, int H,
+               int KV, int D, int n_ctx, long long seq_stride, int kv_dtype, float scale,
+               int max_len, int split_rows, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int ns = 0;
+  float *part_o = nullptr, *part_ml = nullptr;
+  const int rc = decode_split_phase(q, k_cache, v_cache, lens_dev, out, workspace,
+                                    workspace_bytes, B, H, KV, D, n_ctx, seq_stride, kv_dtype,
+                                    scale, max_len, &split_rows, &ns, &part_o, &part_ml, st);
+  if (rc) return rc;
+  const int smem = ns * static_cast<int>(sizeof(float));
   cudaError_t e = b2a_host::launch(decode_combine_kernel, dim3(B * H), dim3(kCombineThreads), smem,
                                    st, part_o, part_ml, lens_dev, out, lse_out, H, D, split_rows,
                                    ns, max_len);

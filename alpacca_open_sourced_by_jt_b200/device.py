@@ -127,6 +127,56 @@ def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, lens: 
     return out
 
 
+def decode_sharded(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor,
+                   lens: torch.Tensor, peer_table: torch.Tensor, rank: int, world: int, *,
+                   scale: float | None = None, max_len: int | None = None, out=None, lse=None,
+                   workspace=None, split_rows: int = 0, stream=None) -> torch.Tensor:
+    """Long-context decode with the KV rows sharded over `world` GPUs
+    (b2a_decode_sharded): this rank's split-KV decode over its rows, then
+    one kernel that pushes the rank's (o, lse) rows into every rank's
+    exchange buffer over NVLink and merges all ranks' parts.  Arguments as
+    in decode() for this rank's rows; peer_table is the int64 device tensor
+    of the ranks' exchange-buffer addresses (longctx.PeerExchange).  Every
+    rank must make the same call; the merged (B, H, D) f32 output is the
+    same on every rank."""
+    if k_shard.dim() == 3:
+        k_shard = k_shard.unsqueeze(0)
+        v_shard = v_shard.unsqueeze(0)
+    _need(q.dim() == 3 and q.dtype == torch.float32 and q.is_cuda and q.is_contiguous(),
+          "q must be a contiguous CUDA f32 tensor (B, H, D)")
+    B, H, D = q.shape
+    _need(k_shard.dim() == 4 and k_shard.shape == v_shard.shape, "k/v shard shape mismatch")
+    _need(k_shard.dtype == v_shard.dtype, "k/v shard dtype mismatch")
+    Bc, n_ctx, KV, Dc = k_shard.shape
+    _need(Bc == B and Dc == D, f"shard {tuple(k_shard.shape)} does not match q {tuple(q.shape)}")
+    _need(k_shard[0].is_contiguous() and v_shard[0].is_contiguous(),
+          "each sequence's shard block must be contiguous")
+    _need(k_shard.stride(0) == v_shard.stride(0), "k/v shards need the same sequence stride")
+    _need(lens.dtype == torch.int32 and lens.is_cuda and lens.numel() == B,
+          "lens must be a CUDA int32 tensor (B,)")
+    _need(peer_table.dtype == torch.int64 and peer_table.is_cuda and
+          peer_table.numel() == world, "peer_table must be a CUDA int64 tensor (world,)")
+    seq_stride = k_shard.stride(0) if B > 1 else n_ctx * KV * D
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if max_len is None:
+        max_len = n_ctx
+    if split_rows <= 0:
+        split_rows = decode_split_rows(B, KV, max_len, k_shard.dtype)
+    if out is None:
+        out = torch.empty((B, H, D), dtype=torch.float32, device=q.device)
+    if workspace is None:
+        workspace = decode_workspace(B, H, D, max_len, split_rows, q.device)
+    if lse is not None:
+        _need(lse.dtype == torch.float32 and lse.numel() == B * H, "lse must be f32 (B, H)")
+    _lib.check(_lib.load().b2a_decode_sharded(
+        _ptr(q), _ptr(k_shard), _ptr(v_shard), _ptr(lens), _ptr(out), _ptr(lse),
+        _ptr(workspace), workspace.numel() * workspace.element_size(), B, H, KV, D, n_ctx,
+        seq_stride, _code(k_shard.dtype), float(scale), int(max_len), int(split_rows),
+        _ptr(peer_table), int(rank), int(world), _stream(stream)))
+    return out
+
+
 def lse_combine(o_parts: torch.Tensor, lse_parts: torch.Tensor, *, out=None, lse=None,
                 stream=None) -> torch.Tensor:
     """Merge G normalised partial outputs (G, R, D) by their lse (G, R).

@@ -14,12 +14,24 @@ empty for a sequence contributes lse = -inf and weight 0.  The exchange is
 B*H*(D+1)*4 bytes per rank (133 KB for 4 sequences x 64 heads x 128), so the
 step is latency-bound, not bandwidth-bound.
 
+Two exchanges are provided:
+  "p2p"   (default on GPUs) one fused kernel (b2a_decode_sharded) merges the
+          rank's split partials, stores its (o, lse) rows straight into
+          every rank's exchange buffer over NVLink (plain peer stores through
+          CUDA-IPC mappings set up once by PeerExchange), waits for the
+          other ranks' rows and merges them: no collective call, one launch
+          after the split kernel, and the step can be replayed as a CUDA
+          graph (`graph()`).
+  "nccl"  the decode with lse, one NCCL all_gather_into_tensor of the
+          packed parts, and the LSE-combine kernel.
 The host logic (row ranges, gather, ordering) is independent of the device
 kernels: `partial_fn` and `combine_fn` default to the B200 kernels and can be
-replaced (the CPU tests run it on gloo ranks with the NumPy oracle).
+replaced (the CPU tests run the "nccl" exchange on gloo ranks with the NumPy
+oracle).
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable
 
 import torch
@@ -57,6 +69,64 @@ def _gpu_combine(o_all, lse_all, out):
     device.lse_combine(o_all, lse_all, out=out)
 
 
+class PeerExchange:
+    """Every rank's exchange buffer for b2a_decode_sharded, mapped into this
+    process.  Each rank allocates its buffer (b2a_shard_exchange_bytes,
+    zeroed), publishes its CUDA-IPC handle with one all-gather, opens the
+    others' handles (peer access over NVLink) and keeps a device table of
+    the G buffer addresses.  Construction is collective: every rank of
+    `group` must build one with the same (B, H, D), and a barrier at the end
+    makes sure every buffer is zeroed and mapped before any rank's first
+    step writes into it."""
+
+    def __init__(self, B: int, H: int, D: int, group=None, device=None):
+        from . import _lib
+        lib = _lib.load()
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.shape = (B, H, D)
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        nbytes = int(lib.b2a_shard_exchange_bytes(B, H, D, self.world))
+        if nbytes <= 0:
+            raise ValueError("bad exchange shape")
+        self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        handle = (ctypes.c_char * 64)()
+        offset = ctypes.c_longlong(0)
+        _lib.check(lib.b2a_ipc_handle(self.buf.data_ptr(), handle, ctypes.byref(offset)))
+        rec = bytes(handle) + int(offset.value).to_bytes(8, "little", signed=True)
+        mine = torch.frombuffer(bytearray(rec), dtype=torch.uint8).to(dev)
+        every = torch.empty((self.world, len(rec)), dtype=torch.uint8, device=dev)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        every = every.cpu().numpy()
+        self._bases = []
+        addrs = []
+        for g in range(self.world):
+            if g == self.rank:
+                addrs.append(self.buf.data_ptr())
+                continue
+            h = bytes(every[g, :64])
+            off = int.from_bytes(bytes(every[g, 64:72]), "little", signed=True)
+            base, ptr = ctypes.c_void_p(), ctypes.c_void_p()
+            _lib.check(lib.b2a_ipc_open(h, off, ctypes.byref(base), ctypes.byref(ptr)))
+            self._bases.append(base.value)
+            addrs.append(ptr.value)
+        self.table = torch.tensor(addrs, dtype=torch.int64, device=dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=group)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (collective: no rank may still be
+        stepping)."""
+        from . import _lib
+        lib = _lib.load()
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for b in self._bases:
+            _lib.check(lib.b2a_ipc_close(b))
+        self._bases = []
+
+
 class LongContextDecoder:
     """Decode one query token per sequence over a KV cache whose rows are
     sharded across the ranks of `group`.
@@ -67,16 +137,43 @@ class LongContextDecoder:
     kernel reads the gathered parts in place through their strides."""
 
     def __init__(self, group=None, partial_fn: Callable | None = None,
-                 combine_fn: Callable | None = None):
+                 combine_fn: Callable | None = None, exchange: str = "nccl"):
         self.group = group
         if dist.is_available() and dist.is_initialized():
             self.rank = dist.get_rank(group)
             self.world = dist.get_world_size(group)
         else:  # single process: one shard holding every row
             self.rank, self.world = 0, 1
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError(f"exchange must be 'nccl' or 'p2p', not {exchange!r}")
+        if exchange == "p2p" and (partial_fn or combine_fn):
+            raise ValueError("the p2p exchange runs the fused device kernel only")
+        if exchange == "p2p" and self.world > 1 and dist.get_backend(group) != "nccl":
+            raise ValueError("the p2p exchange needs GPU ranks (an nccl process group)")
+        self.exchange = exchange
         self.partial_fn = partial_fn or _gpu_partial
         self.combine_fn = combine_fn or _gpu_combine
         self._bufs = {}
+        self._peers = {}
+        self._ws = {}
+
+    def peers(self, B: int, H: int, D: int, device) -> "PeerExchange | None":
+        """The exchange buffers for this shape (built collectively on first
+        use; every rank must reach this call)."""
+        key = (B, H, D, str(device))
+        px = self._peers.get(key)
+        if px is None:
+            if self.world == 1:
+                px = _SoloExchange(B, H, D, device)
+            else:
+                px = PeerExchange(B, H, D, group=self.group, device=device)
+            self._peers[key] = px
+        return px
+
+    def close(self) -> None:
+        for px in self._peers.values():
+            px.close()
+        self._peers = {}
 
     def rows(self, length: int) -> tuple[int, int]:
         return shard_rows(length, self.rank, self.world)
@@ -103,6 +200,14 @@ class LongContextDecoder:
         R = B * H
         if scale is None:
             scale = D ** -0.5
+        if self.exchange == "p2p":
+            from . import device as _device
+            px = self.peers(B, H, D, q.device)
+            out = self.buffers(B, H, D, q.device)[2]
+            ws = self._workspace(B, H, D, k_shard, max_len)
+            return _device.decode_sharded(q, k_shard, v_shard, lens_shard, px.table, self.rank,
+                                          self.world, scale=scale, max_len=max_len, out=out,
+                                          workspace=ws)
         packed, gathered, out = self.buffers(B, H, D, q.device)
         self.partial_fn(q, k_shard, v_shard, lens_shard, scale, max_len,
                         packed[:R * D].view(B, H, D), packed[R * D:].view(B, H))
@@ -116,3 +221,49 @@ class LongContextDecoder:
         lse_all = gathered[:, R * D:]
         self.combine_fn(o_all, lse_all, out.view(R, D))
         return out
+
+    def _workspace(self, B, H, D, k_shard, max_len):
+        from . import device as _device
+        n_ctx = k_shard.shape[-3]
+        ml = n_ctx if max_len is None else int(max_len)
+        KV = k_shard.shape[-2]
+        key = (B, H, D, KV, ml, k_shard.dtype, str(k_shard.device))
+        ws = self._ws.get(key)
+        if ws is None:
+            split = _device.decode_split_rows(B, KV, ml, k_shard.dtype)
+            ws = self._ws[key] = _device.decode_workspace(B, H, D, ml, split, k_shard.device)
+        return ws
+
+    def graph(self, q, k_shard, v_shard, lens_shard, *, scale=None, max_len=None):
+        """Capture one decode step (p2p exchange) as a CUDA graph and return
+        (replay, out): replay() reruns the step on the current contents of
+        q, the shards and lens_shard (lengths are read on the device), and
+        out holds the merged rows.  Collective like decode(): every rank
+        captures, and replays, the same steps in the same order.  The
+        capture runs one step (warm-up) eagerly first."""
+        if self.exchange != "p2p":
+            raise ValueError("graph() captures the p2p exchange (no collective in the graph)")
+        out = self.decode(q, k_shard, v_shard, lens_shard, scale=scale, max_len=max_len)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                self.decode(q, k_shard, v_shard, lens_shard, scale=scale, max_len=max_len)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        return g.replay, out
+
+
+class _SoloExchange:
+    """The one-rank case of PeerExchange: this process's own buffer only."""
+
+    def __init__(self, B, H, D, device):
+        from . import _lib
+        n = int(_lib.load().b2a_shard_exchange_bytes(B, H, D, 1))
+        self.buf = torch.zeros(n, dtype=torch.uint8, device=device)
+        self.table = torch.tensor([self.buf.data_ptr()], dtype=torch.int64, device=device)
+
+    def close(self) -> None:
+        pass

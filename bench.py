@@ -13,10 +13,14 @@ Also reported on the same line:
   prefill   BASELINE config 2 causal prefill (S=2048, 32/8 heads, D=128,
             bf16 in/out) in TFLOP/s, flops = 4*H*D*S(S+1)/2, L2 flushed
             between launches (inputs are 24 MB)
-  varlen    BASELINE config 3: 64 sequences of ragged length (1K-8K), fp16
-            KV, fused RoPE+append then decode, GB/s
-  longctx   BASELINE config 4: 4 x 131072 rows split over the GPUs, NCCL
-            all-gather of (o, lse) parts + LSE combine, GB/s
+  varlen    BASELINE config 3: one batch of 64 sequences of ragged length
+            (1K-8K), sharded by sequence over the GPUs, fp16 KV, fused
+            RoPE+append then decode, GB/s
+  longctx   BASELINE config 4: 4 x 131072 rows split over the GPUs; one CUDA
+            graph per step: local split-KV decode, then one kernel that
+            exchanges the ranks' (o, lse) rows over NVLink peer memory and
+            merges them (the NCCL all-gather path and the one-GPU decode
+            beside it, with the efficiency value_N / (N value_1)), GB/s
   kvstate   KV state boundary: device widening/narrowing of one 32K-row bf16
             layer (HBM GB/s) and a whole-layer f32 snapshot
   qwen35_layer  Qwen35 full-attention layer step (prologue, decode, gate) at
@@ -35,11 +39,13 @@ Also reported on the same line:
   roofline  decode against MEASURED_PEAKS.json's copy bandwidth
   cpu_baseline  the reference's NumPy decode (oracle port) on host cores
 
-Multi-GPU (torchrun, one rank per GPU): every rank decodes its own batch of
-16 sequences (sequence sharding, no collective on the data path), so
-scaling is weak; timing is the max over ranks of CUDA-event time.  The
-single-GPU legs (kvstate, qwen35_layer, decode_step, prefill_chunk, gemm)
-run only when the job has one GPU.
+Multi-GPU (torchrun, one rank per GPU): for the headline every rank decodes
+its own batch of 16 sequences (sequence sharding, no collective on the data
+path), so its scaling is weak; config 3 shards one batch of 64 sequences and
+config 4 shards the rows of 4 sequences (strong scaling).  Timing is the max
+over ranks of CUDA-event time; e2e runs on every rank at once and takes the
+slowest rank's step.  The single-GPU legs (kvstate, qwen35_layer,
+decode_step, prefill_chunk, gemm) run only when the job has one GPU.
 
 `--impl reference` times the reference's CPU implementation (the NumPy
 restatement in oracle/, the reference itself being Python that does not
@@ -207,12 +213,40 @@ def bench_decode(dev, rank, steps, warmup, dist):
     return dict(ms=ms, split=split, kc=kc, vc=vc, q=q, lens=lens, ws=ws, out=out)
 
 
+def _timed_steps(fn, nsteps, dev, dist):
+    """CUDA-event time of nsteps calls of fn on this rank, then the max over
+    ranks (ms); barrier + synchronize on both sides."""
+    import torch
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(nsteps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    return ms
+
+
 def bench_longctx(dev, rank, world, steps, warmup, dist):
     """4 sequences x 131072 rows, 64 q / 8 KV heads, D=128,
-    bf16; the KV rows of every sequence are split across the ranks, each rank
-    decodes its rows, one NCCL all-gather moves the (o, lse) parts and the
-    LSE-combine kernel merges them.  Total work is fixed (strong scaling)."""
+    bf16; the KV rows of every sequence are split across the ranks (strong
+    scaling).  One step, replayed as a CUDA graph: the split-KV decode of the
+    rank's rows, then b2a_decode_sharded's fused kernel (split merge, NVLink
+    peer stores of the rank's (o, lse) rows into every rank's exchange
+    buffer, bounded flag waits, LSE merge).  Beside it: the same step with an
+    NCCL all-gather + LSE-combine kernel instead (eager), and the whole
+    unsharded decode on one GPU, for the efficiency value_N / (N value_1)."""
     import torch
+    from alpacca_open_sourced_by_jt_b200 import device
     from alpacca_open_sourced_by_jt_b200.longctx import LongContextDecoder, shard_rows
     B, L, H, KV, D = LC["B"], LC["L"], LC["H"], LC["KV"], LC["D"]
     a, b = shard_rows(L, rank, world)
@@ -223,53 +257,78 @@ def bench_longctx(dev, rank, world, steps, warmup, dist):
     gq = torch.Generator(device=dev).manual_seed(3)
     q = torch.randn((B, H, D), device=dev, dtype=torch.float32, generator=gq)
     lens = torch.full((B,), n, dtype=torch.int32, device=dev)
-    dec = LongContextDecoder()
+    nsteps = max(10, min(steps, 500))
+    per_step = decode_bytes(B, L, KV, D)
 
-    def step():
-        dec.decode(q, ks, vs, lens, max_len=n)
-
+    dec = LongContextDecoder(exchange="p2p")
+    replay, _ = dec.graph(q, ks, vs, lens, max_len=n)
     for _ in range(max(warmup, 3)):
-        step()
-    torch.cuda.synchronize()
+        replay()
+    ms = _timed_steps(replay, nsteps, dev, dist)
+    del replay
+    dec.close()
+    res = {"metric": "long-context split decode KV GB/s (config 4)",
+           "value": round(per_step / (ms / nsteps * 1e-3) / 1e9, 1), "unit": "GB/s",
+           "ms_per_step": round(ms / nsteps, 4), "steps": nsteps, "n_gpus": world,
+           "scaling": "strong", "gpu_launches_per_step": 2,
+           "config": "4 seqs x 131072 rows (split over the GPUs), 64 q / 8 KV heads, D=128, "
+                     "bf16; per step (one CUDA graph): split-KV decode of the local rows, "
+                     "then one kernel that merges the splits, stores each rank's (o, lse) "
+                     "rows into every rank's buffer over NVLink and merges the ranks' parts"}
+    if world > 1:
+        ndec = LongContextDecoder(exchange="nccl")
+        call = lambda: ndec.decode(q, ks, vs, lens, max_len=n)  # noqa: E731
+        for _ in range(max(warmup, 3)):
+            call()
+        ms_n = _timed_steps(call, nsteps, dev, dist)
+        res["nccl_exchange"] = {
+            "value": round(per_step / (ms_n / nsteps * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "ms_per_step": round(ms_n / nsteps, 4),
+            "path": "eager: decode with lse, NCCL all_gather_into_tensor of the packed "
+                    "parts, LSE-combine kernel"}
+    del ks, vs
+    # the unsharded decode on one GPU (rank 0), the N = 1 point of the curve
+    if rank == 0:
+        torch.cuda.empty_cache()
+        g1 = torch.Generator(device=dev).manual_seed(3)
+        kf = torch.randn((B, L, KV, D), device=dev, dtype=torch.bfloat16, generator=g1)
+        vf = torch.randn((B, L, KV, D), device=dev, dtype=torch.bfloat16, generator=g1)
+        lf = torch.full((B,), L, dtype=torch.int32, device=dev)
+        split = device.decode_split_rows(B, KV, L, torch.bfloat16)
+        ws = device.decode_workspace(B, H, D, L, split, dev)
+        of = torch.empty((B, H, D), dtype=torch.float32, device=dev)
+        one = lambda: device.decode(q, kf, vf, lf, out=of, workspace=ws, split_rows=split)  # noqa: E731
+        for _ in range(3):
+            one()
+        ms1 = _timed_steps(one, nsteps, dev, None)
+        v1 = per_step / (ms1 / nsteps * 1e-3) / 1e9
+        res["single_gpu_value"] = round(v1, 1)
+        res["efficiency"] = round(res["value"] / (world * v1), 4)
+        del kf, vf
+        torch.cuda.empty_cache()
     if dist is not None:
         dist.barrier()
-    torch.cuda.synchronize()
-    nsteps = max(10, min(steps, 500))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(nsteps):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    if dist is not None:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    del ks, vs
-    per_step = decode_bytes(B, L, KV, D)
-    return {"metric": "long-context split decode KV GB/s (config 4)",
-            "value": round(per_step / (ms / nsteps * 1e-3) / 1e9, 1), "unit": "GB/s",
-            "ms_per_step": round(ms / nsteps, 4), "steps": nsteps, "n_gpus": world,
-            "scaling": "strong",
-            "config": "4 seqs x 131072 rows (split over the GPUs), 64 q / 8 KV heads, D=128, "
-                      "bf16; per step: decode of local rows with lse, one NCCL all-gather of "
-                      "B*H*(D+1) f32 per rank, LSE-combine kernel"}
+    return res
 
 
 def bench_varlen(dev, rank, world, steps, warmup, dist):
-    """64 sequences per GPU with cached lengths
+    """one batch of 64 sequences with cached lengths
     L_b ~ U[1024, 8192] (seed 2), 32 q / 8 KV heads, D=128, fp16 KV ~ N(0,1)
-    (seed 2 + rank).  One step is the device half of a batched decode token:
-    the fused RoPE + append kernel rotates every sequence's new q/k row at
-    position L_b and stores k/v there, then the split-KV decode (split +
-    combine kernels) attends over L_b + 1 rows.  Bytes per step: the KV rows
-    read, sum_b 2*(L_b+1)*KV*D*2, plus the new rows and q/out traffic."""
+    (seed 2 + rank), sharded by sequence over the GPUs (rank r holds
+    sequences r, r + N, ...; no collective).  One step is the device half of
+    a batched decode token: the fused RoPE + append kernel rotates every
+    sequence's new q/k row at position L_b and stores k/v there, then the
+    split-KV decode (split + combine kernels) attends over L_b + 1 rows.
+    Bytes per step: the KV rows read, sum_b 2*(L_b+1)*KV*D*2, plus the new
+    rows and q/out traffic, over the whole batch; the time is the max over
+    ranks (strong scaling)."""
     import numpy as np
     import torch
     from alpacca_open_sourced_by_jt_b200 import device
-    B, H, KV, D = VL["B"], VL["H"], VL["KV"], VL["D"]
-    Ls = np.random.default_rng(2).integers(VL["Lmin"], VL["Lmax"] + 1, size=B)
+    H, KV, D = VL["H"], VL["KV"], VL["D"]
+    Ls_all = np.random.default_rng(2).integers(VL["Lmin"], VL["Lmax"] + 1, size=VL["B"])
+    Ls = Ls_all[rank::world]
+    B = len(Ls)
     n_ctx = VL["Lmax"] + 1
     g = torch.Generator(device=dev).manual_seed(2 + rank)
     kc = torch.randn((B, n_ctx, KV, D), device=dev, dtype=torch.float16, generator=g)
@@ -308,19 +367,22 @@ def bench_varlen(dev, rank, world, steps, warmup, dist):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    kv_bytes = int(sum(2 * (int(L) + 1) * KV * D * 2 for L in Ls))
-    extra = B * 2 * KV * D * (4 + 2) + B * H * D * 4 * 4   # new rows in/out; q, q_rot x2, out
+    Bt = VL["B"]
+    kv_bytes = int(sum(2 * (int(L) + 1) * KV * D * 2 for L in Ls_all))
+    extra = Bt * 2 * KV * D * (4 + 2) + Bt * H * D * 4 * 4  # new rows in/out; q, q_rot x2, out
     per_step = kv_bytes + extra
+    local = int(sum(2 * (int(L) + 1) * KV * D * 2 for L in Ls)) + extra * B // Bt
     del kc, vc
     return {"metric": "varlen batched decode GB/s (config 3)",
-            "value": round(world * per_step / (ms / nsteps * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "value": round(per_step / (ms / nsteps * 1e-3) / 1e9, 1), "unit": "GB/s",
             "ms_per_step": round(ms / nsteps, 4), "steps": nsteps, "n_gpus": world,
-            "scaling": "weak", "bytes_per_step_per_gpu": per_step, "split_rows": split,
-            "gpu_launches_per_step": 3,
-            "config": "64 seqs per GPU, L_b ~ U[1024,8192] (seed 2; mean "
-                      f"{float(Ls.mean()):.0f}), 32 q / 8 KV heads, D=128, fp16 KV; per step: "
-                      "fused RoPE+append of each new token at L_b, split-KV decode over "
-                      "L_b+1 rows; KV bytes > L2, no flush"}
+            "scaling": "strong", "bytes_per_step": per_step, "split_rows": split,
+            "seqs_per_gpu": B, "gpu_launches_per_step": 3,
+            "achieved_per_gpu_max": round(local / (ms / nsteps * 1e-3) / 1e9, 1),
+            "config": "one batch of 64 seqs sharded by sequence over the GPUs, L_b ~ "
+                      f"U[1024,8192] (seed 2; mean {float(Ls_all.mean()):.0f}), 32 q / 8 KV "
+                      "heads, D=128, fp16 KV; per step: fused RoPE+append of each new token "
+                      "at L_b, split-KV decode over L_b+1 rows; KV bytes > L2, no flush"}
 
 
 def bench_kvstate(dev, steps, warmup):
@@ -617,7 +679,7 @@ def bench_prefill_chunk(dev, steps, warmup):
                       "tcgen05 causal prefill; eager launches (7 per layer)"}
 
 
-def bench_e2e(dev, st, steps, warmup):
+def bench_e2e(dev, st, steps, warmup, dist=None):
     """Decode step through the public API with host buffers (see module doc):
     DecodeStep replays the whole step (H2D of the pinned rows, fused
     RoPE+append, decode, D2H of the output) as one CUDA graph per token."""
@@ -637,14 +699,22 @@ def bench_e2e(dev, st, steps, warmup):
     for _ in range(max(warmup, 3)):
         step()
     n = max(3, min(steps, 500))
+    world = 1
+    if dist is not None:
+        world = dist.get_world_size()
+        dist.barrier()
     t0 = time.perf_counter()
     for _ in range(n):
         out = step()
     dt = time.perf_counter() - t0
-    bytes_step = decode_bytes(B, L, KV, D)
-    return dict(value=bytes_step / (dt / n) / 1e9, unit="GB/s",
-                h2d_bytes_per_step=int((B * H * D + 2 * B * KV * D) * 4 + 2 * B * 4),
-                d2h_bytes_per_step=int(out.numel() * 4), steps=n,
+    if dist is not None:
+        t = torch.tensor([dt], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    bytes_step = decode_bytes(B, L, KV, D) * world
+    return dict(value=bytes_step / (dt / n) / 1e9, unit="GB/s", ranks_timed=world,
+                h2d_bytes_per_step=world * int((B * H * D + 2 * B * KV * D) * 4 + 2 * B * 4),
+                d2h_bytes_per_step=world * int(out.numel() * 4), steps=n,
                 ms_per_step=dt / n * 1e3,
                 path="DecodeStep: one CUDA graph per token (pinned q/k/v/positions H2D, "
                      "fused RoPE+append into the resident cache, split-KV decode, output "
@@ -781,11 +851,12 @@ def run_ours(args):
     hbm, bf16, bf16_sus, src = peaks()
     achieved = per_step / (ms / args.steps * 1e-3) / 1e9   # per rank, per launch pair
     result = None
+    e2e = None
+    if args.only in (None, "e2e"):
+        # every rank runs its own end-to-end loop at the same time; the
+        # slowest rank's step time counts for all
+        e2e = bench_e2e(dev, st, args.steps, args.warmup, dist)
     if rank == 0:
-        e2e = None
-        if args.only in (None, "e2e"):
-            e2e = bench_e2e(dev, st, args.steps, args.warmup)
-            e2e["value"] *= world
         pf = None
         if args.only in (None, "prefill") and not args.no_prefill:
             pf = bench_prefill(dev, args.steps, args.warmup)
@@ -826,9 +897,10 @@ def run_ours(args):
         if gmm:
             result["gemm"] = gmm
         if vl:
-            vl["roofline"] = {"bound": "hbm", "achieved": round(vl["value"] / world, 1),
-                              "peak": hbm, "unit": "GB/s",
-                              "frac": round(vl["value"] / world / hbm, 4)}
+            ach = vl["achieved_per_gpu_max"] if world > 1 else vl["value"]
+            vl["roofline"] = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                              "frac": round(ach / hbm, 4),
+                              "note": "rank 0's bytes over the max-over-ranks step time"}
             result["varlen"] = vl
         if cpu:
             result["cpu_baseline"] = cpu

@@ -145,6 +145,56 @@ int b2a_lse_combine(const float* o_parts, long long o_part_stride, const float* 
                     long long lse_part_stride, int G, int rows, int D, float* out,
                     float* lse_out, void* stream);
 
+/* ---- long-context decode sharded across GPUs ---------------------------
+ *
+ * The KV rows of every sequence are split into contiguous ranges, one per
+ * GPU (rank); each rank calls b2a_decode_sharded on its range and every
+ * rank receives the merged result.  Replaces, for a context too long for
+ * one GPU, b2a_decode followed by an all-gather of the per-rank (o, lse)
+ * parts and b2a_lse_combine: the algebra of _attention_decode_combine
+ * (alpaccaroo/cuda.py:674-694) lifted from split CTAs to ranks.  The
+ * reference has no multi-GPU decode; this is the natural shard of its
+ * split-KV decode.
+ *
+ * One kernel after the split kernel merges this rank's splits per row,
+ * stores the row (o, lse) into every rank's exchange buffer over NVLink
+ * (plain peer stores through CUDA-IPC mappings), publishes a per-row flag
+ * with a system-scope release, waits for every rank's flag (bounded: on
+ * expiry B2A_ERR_TIMEOUT is recorded) and merges the G parts by their lse.
+ *
+ *   q, k_shard, v_shard, lens_dev, out, lse_out, workspace, sizes, dtype,
+ *   scale, max_len, split_rows  as in b2a_decode, over this rank's rows
+ *   peer_xbufs_dev  device array [G] of pointers: rank g's exchange buffer
+ *                   as mapped in this process (this rank's own at [rank])
+ *   rank, G         this rank and the number of ranks (G <= 128)
+ * Exchange buffers: b2a_shard_exchange_bytes(B, H, D, G) bytes per rank,
+ * zeroed once, then mapped by every rank (b2a_ipc_handle / b2a_ipc_open)
+ * before any rank's first call.  Every rank makes the same sequence of
+ * calls with the same B, H and D; a rank's call completes only when every
+ * rank's call for the same step has published its rows, so the G calls of
+ * a step must be able to run at the same time (one process per GPU).  The
+ * call can be captured in a CUDA graph (step counters live on the device). */
+size_t b2a_shard_exchange_bytes(int B, int H, int D, int G);
+int b2a_decode_sharded(const float* q, const void* k_shard, const void* v_shard,
+                       const int* lens_dev, float* out, float* lse_out, void* workspace,
+                       size_t workspace_bytes, int B, int H, int KV, int D, int n_ctx,
+                       long long seq_stride, int kv_dtype, float scale, int max_len,
+                       int split_rows, void* const* peer_xbufs_dev, int rank, int G,
+                       void* stream);
+
+/* CUDA IPC plumbing for the exchange buffers (set-up only; no reference
+ * counterpart).  b2a_ipc_handle writes the B2A_IPC_HANDLE_BYTES-byte handle
+ * of the allocation holding dev_ptr and dev_ptr's offset inside it;
+ * b2a_ipc_open maps a peer process's handle (peer access enabled lazily)
+ * and returns the mapping's base and base + offset; b2a_ipc_close unmaps a
+ * base returned by b2a_ipc_open.  The allocation must come from cudaMalloc
+ * (PyTorch's default caching allocator qualifies; expandable segments do
+ * not). */
+#define B2A_IPC_HANDLE_BYTES 64
+int b2a_ipc_handle(const void* dev_ptr, void* handle_out, long long* offset_out);
+int b2a_ipc_open(const void* handle, long long offset, void** base_out, void** ptr_out);
+int b2a_ipc_close(void* base);
+
 /* ---- (2) causal prefill on tcgen05 --------------------------------------
  *
  * Replaces Model._attention_batch_np (alpaccaroo/model.py:1254-1272), its
