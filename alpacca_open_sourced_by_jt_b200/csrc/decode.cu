@@ -26,6 +26,7 @@
 #include <math.h>
 
 #include "b2a_common.cuh"
+#include "shard_words.cuh"
 
 namespace b2a {
 namespace decode {
@@ -57,13 +58,72 @@ constexpr int smem_bytes() {
 }
 
 // ---------------------------------------------------------------------------
+// Sharded decode: the last split CTA of a (sequence, KV head) merges the
+// group's splits and publishes the rows to every rank (shard.cu)
+// ---------------------------------------------------------------------------
+// Called by the 128 consumer threads after the CTA wrote its partials.  The
+// CTAs of one (sequence, KV head) take tickets; the one that draws the last
+// ticket has every partial of the group visible (each CTA fences its
+// partial stores before its ticket), merges the splits of each head and
+// stores the (value, tag) words of the rows into slot [me] of every rank's
+// exchange buffer.  Ranks whose share of a sequence is empty publish from
+// the collect kernel instead (no split CTA runs for them).
+template <int D>
+__device__ __noinline__ void publish_group(const shard::Publish pub, const float* part_o,
+                                           const float* part_ml, int b, int kvh, int H,
+                                           int group, int len, int split_rows, int n_splits) {
+  __shared__ int s_last;
+  __threadfence();
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32));
+  const int R = static_cast<int>(gridDim.z) * H;
+  const shard::XLayout xl = shard::xlayout(R, D, pub.G);
+  unsigned char* mine = pub.peers[pub.me];
+  uint32_t* counts = reinterpret_cast<uint32_t*>(mine + xl.counts);
+  const uint32_t* steps = reinterpret_cast<const uint32_t*>(mine + xl.steps);
+  const int ns_b = min(n_splits, (len + split_rows - 1) / split_rows);
+  const int slot = b * static_cast<int>(gridDim.y) + kvh;
+  if (threadIdx.x == 0) {
+    const unsigned t = atomicAdd(&counts[slot], 1u);
+    s_last = (t == static_cast<unsigned>(ns_b - 1)) ? 1 : 0;
+    if (s_last) counts[slot] = 0u;  // every CTA of the group has drawn its ticket
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32));
+  if (!s_last) return;
+  __threadfence();
+  const int r0 = b * H + kvh * group;
+  for (int idx = threadIdx.x; idx < group * (D + 1); idx += kConsumerWarps * 32) {
+    const int n = idx / (D + 1), d = idx - n * (D + 1);
+    const size_t p0 = static_cast<size_t>(r0 + n) * n_splits;
+    float M = -INFINITY;
+    for (int sp = 0; sp < ns_b; ++sp) M = fmaxf(M, __ldcg(part_ml + (p0 + sp) * 2));
+    const float Mref = (M == -INFINITY) ? 0.f : M;
+    float L = 0.f, acc = 0.f;
+    for (int sp = 0; sp < ns_b; ++sp) {
+      const float w = exp2f(__ldcg(part_ml + (p0 + sp) * 2) - Mref);
+      L += __ldcg(part_ml + (p0 + sp) * 2 + 1) * w;
+      if (d < D) acc += __ldcg(part_o + (p0 + sp) * D + d) * w;
+    }
+    const float val = d < D ? (L > 0.f ? acc / L : 0.f)
+                            : (L > 0.f ? (Mref + log2f(L)) * 0.6931471805599453f : -INFINITY);
+    const int r = r0 + n;
+    const uint32_t step = __ldcg(steps + r);
+    for (int g = 0; g < pub.G; ++g) {
+      uint2* dst = reinterpret_cast<uint2*>(pub.peers[g] + xl.words) +
+                   shard::word_index(static_cast<int>(step & 1u), pub.me, r, R, pub.G, D);
+      shard::st_tagged(dst + d, val, step + 1u);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Tensor-core kernel (f16 / bf16 caches)
 // ---------------------------------------------------------------------------
 template <typename T, int D, int NT>
 __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
     const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
     const float* __restrict__ q, const int* __restrict__ lens, float* __restrict__ part_o,
-    float* __restrict__ part_ml, int H, int group, int split_rows, int n_splits, float qscale) {
+    float* __restrict__ part_ml, int H, int group, int split_rows, int n_splits, float qscale,
+    const shard::Publish pub) {
   // The kernels after this one (a PDL chain) are released only once every
   // CTA has streamed its rows (end of the main loop, below): released at
   // entry, they would start their own weight prefetches and take HBM
@@ -332,6 +392,8 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
       part_ml[pidx * 2 + 1] = L;
     }
   }
+  if (pub.peers != nullptr) publish_group<D>(pub, part_o, part_ml, b, kvh, H, group, len,
+                                             split_rows, n_splits);
 }
 
 // ---------------------------------------------------------------------------
@@ -588,7 +650,7 @@ size_t part_o_bytes(int B, int H, int D, int n_splits) {
 template <typename T, int D, int NT>
 int launch_mma(const CUtensorMap& tk, const CUtensorMap& tv, const float* q, const int* lens,
                float* part_o, float* part_ml, int B, int H, int KV, int group, int split_rows,
-               int n_splits, float qscale, cudaStream_t st) {
+               int n_splits, float qscale, const b2a::shard::Publish& pub, cudaStream_t st) {
   auto kern = decode_mma_kernel<T, D, NT>;
   constexpr int smem = smem_bytes<D, NT>();
   static unsigned long long configured = 0;  // bit per device: attribute set
@@ -601,7 +663,8 @@ int launch_mma(const CUtensorMap& tk, const CUtensorMap& tv, const float* q, con
   }
   dim3 grid(n_splits, KV, B);
   const cudaError_t e = b2a_host::launch(kern, grid, dim3(Dk::kThreads), smem, st, tk, tv, q, lens,
-                                         part_o, part_ml, H, group, split_rows, n_splits, qscale);
+                                         part_o, part_ml, H, group, split_rows, n_splits, qscale,
+                                         pub);
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "decode launch");
   return B2A_OK;
 }
@@ -609,28 +672,28 @@ int launch_mma(const CUtensorMap& tk, const CUtensorMap& tv, const float* q, con
 template <typename T, int D>
 int dispatch_nt(int group, const CUtensorMap& tk, const CUtensorMap& tv, const float* q,
                 const int* lens, float* po, float* pml, int B, int H, int KV, int split_rows,
-                int n_splits, float qscale, cudaStream_t st) {
+                int n_splits, float qscale, const b2a::shard::Publish& pub, cudaStream_t st) {
   if (group <= 8)
     return launch_mma<T, D, 1>(tk, tv, q, lens, po, pml, B, H, KV, group, split_rows, n_splits,
-                               qscale, st);
+                               qscale, pub, st);
   return launch_mma<T, D, 2>(tk, tv, q, lens, po, pml, B, H, KV, group, split_rows, n_splits,
-                             qscale, st);
+                             qscale, pub, st);
 }
 
 template <typename T>
 int dispatch_d(int D, int group, const CUtensorMap& tk, const CUtensorMap& tv, const float* q,
                const int* lens, float* po, float* pml, int B, int H, int KV, int split_rows,
-               int n_splits, float qscale, cudaStream_t st) {
+               int n_splits, float qscale, const b2a::shard::Publish& pub, cudaStream_t st) {
   switch (D) {
     case 64:
       return dispatch_nt<T, 64>(group, tk, tv, q, lens, po, pml, B, H, KV, split_rows, n_splits,
-                                qscale, st);
+                                qscale, pub, st);
     case 128:
       return dispatch_nt<T, 128>(group, tk, tv, q, lens, po, pml, B, H, KV, split_rows, n_splits,
-                                 qscale, st);
+                                 qscale, pub, st);
     case 256:
       return dispatch_nt<T, 256>(group, tk, tv, q, lens, po, pml, B, H, KV, split_rows, n_splits,
-                                 qscale, st);
+                                 qscale, pub, st);
   }
   return fail(B2A_ERR_UNSUPPORTED, "decode: head_dim %d (tensor-core path takes 64/128/256)", D);
 }
@@ -704,7 +767,9 @@ int decode_split_phase(const float* q, const void* k_cache, const void* v_cache,
                        size_t workspace_bytes, int B, int H, int KV, int D, int n_ctx,
                        long long seq_stride, int kv_dtype, float scale, int max_len,
                        int* split_rows_io, int* ns_out, float** part_o_out, float** part_ml_out,
-                       cudaStream_t st) {
+                       cudaStream_t st, const b2a::shard::Publish& pub = {nullptr, 0, 0},
+                       bool* published = nullptr) {
+  if (published) *published = false;
   if (!q || !k_cache || !v_cache || !lens_dev || !out)
     return fail(B2A_ERR_ARG, "decode: null pointer argument");
   if (B <= 0 || H <= 0 || KV <= 0 || D <= 0 || n_ctx <= 0 || max_len < 0)
@@ -770,10 +835,11 @@ int decode_split_phase(const float* q, const void* k_cache, const void* v_cache,
       if (rc) return rc;
       if (kv_dtype == B2A_BF16)
         rc = dispatch_d<__nv_bfloat16>(D, group, tk, tv, q, lens_dev, part_o, part_ml, B, H, KV,
-                                       split_rows, ns, qscale, st);
+                                       split_rows, ns, qscale, pub, st);
       else
         rc = dispatch_d<__half>(D, group, tk, tv, q, lens_dev, part_o, part_ml, B, H, KV,
-                                split_rows, ns, qscale, st);
+                                split_rows, ns, qscale, pub, st);
+      if (published) *published = pub.peers != nullptr;
     }
     if (rc) return rc;
   }

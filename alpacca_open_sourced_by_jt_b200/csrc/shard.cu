@@ -7,31 +7,37 @@
 // (one (sequence, query head) pair):
 //   phase A  merge this rank's split partials into (o_r, lse_r) (the
 //            algebra of the reference's _attention_decode_combine,
-//            alpaccaroo/cuda.py:674-694), store them into slot [me] of
-//            EVERY rank's exchange buffer with plain stores through the
-//            CUDA-IPC mappings (NVLink peer stores; no TMA, no multicast),
-//            then publish flag[me][r] = step + 1 on every rank with a
-//            system-scope release store;
-//   phase B  wait (acquire loads, bounded by kShardWaitNs) until every
-//            rank's flag[g][r] in this rank's own buffer reached step + 1,
-//            then merge the G parts by their lse:
+//            alpaccaroo/cuda.py:674-694) and store them into slot [me] of
+//            EVERY rank's exchange buffer through the CUDA-IPC mappings
+//            (NVLink peer stores; no TMA, no multicast);
+//   phase B  read every rank's slot of row r from this rank's own buffer and
+//            merge the G parts by their lse:
 //              out_r = sum_g exp(lse_g - L) o_g,  L = log sum_g exp(lse_g)
 // so every rank ends with the merged rows, the result of an all-gather
 // followed by the combine, without a separate collective or launch.
 //
+// No fences and no separate flags: every value travels in an 8-byte word
+// (f32 value, u32 tag) written by one 8-byte store, and the tag is the
+// step number + 1, so a reader that sees the tag it expects sees the value
+// with it (an aligned 8-byte store is not split).  A reader spins on each
+// word until its tag arrives, bounded by kShardWaitNs (on expiry it records
+// B2A_ERR_TIMEOUT and merges what it has).
+//
 // Exchange buffer of each rank (b2a_shard_exchange_bytes, zeroed once
-// before first use): data [2][G][R][D+1] f32 (step parity, source rank,
-// row, o then lse), flags [G][R] u32 (written by the source ranks), steps
-// [R] u32 (this rank's count of finished steps per row).  Double buffering
-// by step parity is enough: a rank can write step n+2 into a slot only after
-// its step n+1 waited for every rank's step n+1 flag, which each rank
-// publishes only after its step n kernel (the last reader of the slot) has
-// completed on its stream.  Rows are independent (per-row flags and step
-// counts), so ranks may use different grids.
+// before first use): words [2][G][R][D+1] (step parity, source rank, row,
+// o then lse) and steps [R] u32 (this rank's count of finished steps per
+// row).  Double buffering by step parity is enough: a rank writes step n+2
+// into a slot only after its step n+1 read every rank's step n+1 words,
+// which each rank writes only after its step n kernel (the last reader of
+// the slot) has completed on its stream.  Tags grow by one per step, so a
+// word left from step n in the same slot never passes for step n+2.
+// Rows are independent, so ranks may use different grids.
 //
 // The grid never exceeds the number of CTAs that can be resident at once,
-// and every CTA finishes phase A for all of its rows before it waits in
-// phase B, so the waits cannot block a CTA that has yet to publish.
+// and every CTA writes all of its rows (phase A) before it waits in phase
+// B, so the waits cannot block a CTA that has yet to write.
+
+#include "shard_words.cuh"
 
 namespace b2a {
 namespace shard {
@@ -42,32 +48,22 @@ constexpr int kThreads = 128;
 // B2A_ERR_TIMEOUT (the kernel then merges what it has and returns).
 constexpr uint64_t kShardWaitNs = 2000000000ull;
 
-struct XLayout {
-  size_t data, flags, steps, total;
-};
-
-__host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
-
-__host__ __device__ inline XLayout xlayout(int R, int D, int G) {
-  XLayout x;
-  x.data = 0;
-  x.flags = align256(static_cast<size_t>(2) * G * R * (D + 1) * sizeof(float));
-  x.steps = x.flags + align256(static_cast<size_t>(G) * R * sizeof(uint32_t));
-  x.total = x.steps + align256(static_cast<size_t>(R) * sizeof(uint32_t));
-  return x;
-}
-
-__device__ __forceinline__ size_t data_index(int parity, int src, int row, int R, int G, int D) {
-  return ((static_cast<size_t>(parity) * G + src) * R + row) * static_cast<size_t>(D + 1);
-}
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+// Spin until the word carries `tag`; returns its value.  *deadline_hit is
+// set (and the error recorded once) when the wait runs past t_end.
+__device__ __forceinline__ float wait_tagged(const uint2* p, uint32_t tag, uint64_t t_end,
+                                             bool* deadline_hit) {
+  uint2 w = ld_tagged(p);
+  if (w.y == tag) return __uint_as_float(w.x);
+  uint32_t spins = 0;
+  while (!*deadline_hit) {
+    w = ld_tagged(p);
+    if (w.y == tag) return __uint_as_float(w.x);
+    if ((++spins & 63u) == 0u && globaltimer_ns() > t_end) {
+      set_dev_error(B2A_ERR_TIMEOUT, 0x50000);
+      *deadline_hit = true;
+    }
+  }
+  return __uint_as_float(w.x);
 }
 
 // Merge row bh's split partials (m in log2 units, l, unnormalised acc) into
@@ -132,90 +128,77 @@ __global__ void __launch_bounds__(kThreads) shard_exchange_kernel(
     const float* __restrict__ part_o, const float* __restrict__ part_ml,
     const int* __restrict__ lens, float* __restrict__ out, float* __restrict__ lse_out,
     unsigned char* const* __restrict__ peers, int me, int G, int R, int H, int D,
-    int split_rows, int n_splits, int row_limit) {
+    int split_rows, int n_splits, int row_limit, int publish_all) {
+  // publish_all: the split kernel did not publish (fp32 caches, or no rows
+  // at all), so this kernel merges and publishes every row and must first
+  // wait for the split partials.  Otherwise it publishes only the rows of
+  // sequences with no local rows (no split CTA ran for them) and starts
+  // while the split kernel's last CTAs are still publishing.
+  if (publish_all) pdl_wait();
   extern __shared__ float ssm[];
   float* wsm = ssm;                 // [n_splits] split weights
   float* obuf = ssm + n_splits;     // [D] this rank's merged row
   __shared__ uint32_t s_step;
-  __shared__ int s_abort;  // a wait of this CTA ran out: later rows do not wait again
   const XLayout xl = xlayout(R, D, G);
-  if (threadIdx.x == 0) s_abort = 0;
   unsigned char* mine = peers[me];
-  uint32_t* flags = reinterpret_cast<uint32_t*>(mine + xl.flags);
   uint32_t* steps = reinterpret_cast<uint32_t*>(mine + xl.steps);
-  const float* data = reinterpret_cast<const float*>(mine + xl.data);
+  const uint2* words = reinterpret_cast<const uint2*>(mine + xl.words);
 
-  // phase A: merge the local splits of each of this CTA's rows and publish
-  // them to every rank
+  // phase A: merge the local splits of each of this CTA's rows and store
+  // them, tagged, into every rank's buffer
   for (int r = blockIdx.x; r < R; r += gridDim.x) {
     const int b = r / H;
     const int len = lens[b];
     if (threadIdx.x == 0 && (len < 0 || len > row_limit)) set_dev_error(B2A_ERR_POSITION, b);
+    if (!publish_all && len > 0) continue;  // the split kernel published this row
     const int ns = (len <= 0) ? 0 : min(n_splits, (len + split_rows - 1) / split_rows);
     if (threadIdx.x == 0) s_step = steps[r];
     const float lse = merge_splits(part_o, part_ml, r, ns, n_splits, D, wsm, obuf);
     const uint32_t step = s_step;
+    const uint32_t tag = step + 1u;
     const int parity = static_cast<int>(step & 1u);
     for (int g = 0; g < G; ++g) {
-      float* dst = reinterpret_cast<float*>(peers[g] + xl.data) + data_index(parity, me, r, R, G, D);
-      for (int d = threadIdx.x; d < D; d += kThreads) dst[d] = obuf[d];
-      if (threadIdx.x == 0) dst[D] = lse;
+      uint2* dst = reinterpret_cast<uint2*>(peers[g] + xl.words) +
+                   word_index(parity, me, r, R, G, D);
+      for (int d = threadIdx.x; d <= D; d += kThreads) st_tagged(dst + d, d < D ? obuf[d] : lse, tag);
     }
-    // every thread's peer stores become visible system-wide before the
-    // flags that announce them
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x < G) {
-      uint32_t* f = reinterpret_cast<uint32_t*>(peers[threadIdx.x] + xl.flags) +
-                    static_cast<size_t>(me) * R + r;
-      st_release_sys(f, step + 1u);
-    }
-    __syncthreads();  // obuf / wsm reused by the next row
+    __syncthreads();  // obuf / wsm / s_step reused by the next row
   }
 
-  // phase B: wait for every rank's part of each row, then merge
+  // phase B: every rank's part of each row, then the merge
+  const uint64_t t_end = globaltimer_ns() + kShardWaitNs;
+  bool hit = false;  // this thread's waits ran out: it stops waiting
   for (int r = blockIdx.x; r < R; r += gridDim.x) {
-    if (threadIdx.x == 0) s_step = steps[r];
-    __syncthreads();
-    const uint32_t step = s_step;
+    const uint32_t step = steps[r];
+    const uint32_t tag = step + 1u;
     const int parity = static_cast<int>(step & 1u);
-    if (threadIdx.x < G && !s_abort) {
-      const uint32_t* f = flags + static_cast<size_t>(threadIdx.x) * R + r;
-      if (static_cast<int>(ld_acquire_sys(f) - (step + 1u)) < 0) {
-        const uint64_t t0 = globaltimer_ns();
-        uint32_t spins = 0;
-        while (static_cast<int>(ld_acquire_sys(f) - (step + 1u)) < 0) {
-          if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > kShardWaitNs) {
-            set_dev_error(B2A_ERR_TIMEOUT, 0x50000 | threadIdx.x);
-            s_abort = 1;
-            break;
-          }
-        }
-      }
-    }
-    __syncthreads();
-    // lse of every part, read through L2 (the slots are rewritten by peers)
     float M = -INFINITY;
     for (int g = 0; g < G; ++g)
-      M = fmaxf(M, __ldcg(data + data_index(parity, g, r, R, G, D) + D));
+      M = fmaxf(M, wait_tagged(words + word_index(parity, g, r, R, G, D) + D, tag, t_end, &hit));
     const float Mref = (M == -INFINITY) ? 0.f : M;
     float L = 0.f;
-    for (int g = 0; g < G; ++g) L += expf(__ldcg(data + data_index(parity, g, r, R, G, D) + D) - Mref);
+    for (int g = 0; g < G; ++g) {
+      const float l = __uint_as_float(ld_tagged(words + word_index(parity, g, r, R, G, D) + D).x);
+      L += expf(l - Mref);
+    }
     const float invL = (L > 0.f) ? 1.f / L : 0.f;
     for (int d = threadIdx.x; d < D; d += kThreads) {
       float acc = 0.f;
       for (int g = 0; g < G; ++g) {
-        const float* src = data + data_index(parity, g, r, R, G, D);
-        acc += expf(__ldcg(src + D) - Mref) * __ldcg(src + d);
+        const uint2* src = words + word_index(parity, g, r, R, G, D);
+        const float w = expf(__uint_as_float(ld_tagged(src + D).x) - Mref);
+        acc += w * wait_tagged(src + d, tag, t_end, &hit);
       }
       out[static_cast<size_t>(r) * D + d] = acc * invL;
     }
+    __syncthreads();  // every thread read steps[r] before it moves on
     if (threadIdx.x == 0) {
       if (lse_out) lse_out[r] = (L > 0.f) ? Mref + logf(L) : -INFINITY;
-      steps[r] = step + 1u;
+      steps[r] = tag;
     }
-    __syncthreads();
   }
+  // finish no earlier than the split kernel (a no-op for an ordinary launch)
+  pdl_wait();
 }
 
 }  // namespace shard
@@ -299,9 +282,11 @@ int b2a_decode_sharded(const float* q, const void* k_shard, const void* v_shard,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int ns = 0;
   float *part_o = nullptr, *part_ml = nullptr;
+  bool published = false;
+  const b2a::shard::Publish pub{reinterpret_cast<unsigned char* const*>(peer_xbufs_dev), rank, G};
   int rc = decode_split_phase(q, k_shard, v_shard, lens_dev, out, workspace, workspace_bytes, B,
                               H, KV, D, n_ctx, seq_stride, kv_dtype, scale, max_len, &split_rows,
-                              &ns, &part_o, &part_ml, st);
+                              &ns, &part_o, &part_ml, st, pub, &published);
   if (rc) return rc;
   namespace S = b2a::shard;
   auto kern = S::shard_exchange_kernel;
@@ -311,13 +296,29 @@ int b2a_decode_sharded(const float* q, const void* k_shard, const void* v_shard,
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "decode_sharded: occupancy");
   if (occ < 1) return fail(B2A_ERR_UNSUPPORTED, "decode_sharded: exchange kernel cannot be resident");
   const int R = B * H;
-  const int resident = occ * b2a_host::sm_count();
-  const int grid = R < resident ? R : resident;  // every CTA resident: the waits cannot starve
-  kern<<<grid, S::kThreads, smem, st>>>(
-      part_o, part_ml, lens_dev, out, lse_out,
-      reinterpret_cast<unsigned char* const*>(peer_xbufs_dev), rank, G, R, H, D, split_rows, ns,
-      max_len);
-  e = cudaGetLastError();
+  // at most one CTA per SM, never more than can be resident at once, so the
+  // waits cannot starve a CTA that has yet to write its rows
+  const int sms = b2a_host::sm_count();
+  const int resident = occ * sms;
+  int grid = R < sms ? R : sms;
+  if (grid > resident) grid = resident;
+  // a programmatic dependent of the split kernel: its CTAs are resident and
+  // reading the exchange words while the last split CTAs publish
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(S::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, static_cast<const float*>(part_o),
+                         static_cast<const float*>(part_ml), lens_dev, out, lse_out,
+                         reinterpret_cast<unsigned char* const*>(peer_xbufs_dev), rank, G, R, H,
+                         D, split_rows, ns, max_len, published ? 0 : 1);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "decode_sharded launch");
   return B2A_OK;
 }

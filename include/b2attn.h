@@ -158,9 +158,11 @@ int b2a_lse_combine(const float* o_parts, long long o_part_stride, const float* 
  *
  * One kernel after the split kernel merges this rank's splits per row,
  * stores the row (o, lse) into every rank's exchange buffer over NVLink
- * (plain peer stores through CUDA-IPC mappings), publishes a per-row flag
- * with a system-scope release, waits for every rank's flag (bounded: on
- * expiry B2A_ERR_TIMEOUT is recorded) and merges the G parts by their lse.
+ * (plain peer stores through CUDA-IPC mappings, each value in an 8-byte
+ * word with the step number as its tag, so no fence or flag is needed),
+ * waits until every rank's words of the row carry this step's tag
+ * (bounded: on expiry B2A_ERR_TIMEOUT is recorded) and merges the G parts
+ * by their lse.
  *
  *   q, k_shard, v_shard, lens_dev, out, lse_out, workspace, sizes, dtype,
  *   scale, max_len, split_rows  as in b2a_decode, over this rank's rows
