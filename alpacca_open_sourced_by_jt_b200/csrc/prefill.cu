@@ -208,6 +208,62 @@ __device__ __noinline__ void store_mean_v_rows(bool need, TO* orow, const T* __r
   }
 }
 
+// 16 bytes of an output row: 8 16-bit or 4 f32 elements, each times scale.
+template <typename TO>
+__device__ __forceinline__ uint4 pack16(const float* v, float scale) {
+  uint4 u;
+  if constexpr (std::is_same<TO, float>::value) {
+    u.x = __float_as_uint(v[0] * scale);
+    u.y = __float_as_uint(v[1] * scale);
+    u.z = __float_as_uint(v[2] * scale);
+    u.w = __float_as_uint(v[3] * scale);
+  } else {
+    u.x = Pack2<TO>::run(v[0] * scale, v[1] * scale);
+    u.y = Pack2<TO>::run(v[2] * scale, v[3] * scale);
+    u.z = Pack2<TO>::run(v[4] * scale, v[5] * scale);
+    u.w = Pack2<TO>::run(v[6] * scale, v[7] * scale);
+  }
+  return u;
+}
+
+// Epilogue of one warp: the O rows of its 32 TMEM lanes (query rows
+// row_base .. row_base+31 of head h, TMEM address t_o = lane quarter + O
+// column) times inv go to out[row][h][0..D).  Each 128-byte row segment is
+// staged in a 4 KB per-warp shared-memory buffer (16-byte chunks XOR-swizzled
+// by row, conflict-free both ways), then written by 8 lanes per row, so every
+// store instruction covers four whole 128-byte segments instead of 32
+// scattered 16-byte pieces.  Rows whose `good` flag is false are skipped.
+template <typename TO, int D>
+__device__ __forceinline__ void store_o_rows(uint32_t t_o, uint8_t* stg, TO* __restrict__ out,
+                                             int row_base, int H, int h, float inv, bool good) {
+  constexpr int kCols = 128 / static_cast<int>(sizeof(TO));  // columns per 128-byte segment
+  constexpr int kEl = 16 / static_cast<int>(sizeof(TO));     // elements per 16-byte chunk
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int ch = 0; ch < D / kCols; ++ch) {
+    float o[kCols];
+#pragma unroll
+    for (int q = 0; q < kCols / 32; ++q) tc_ld32(t_o + ch * kCols + q * 32, o + q * 32);
+    tc_wait_ld();
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+          pack16<TO>(o + c * kEl, inv);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rr = i * 4 + (lane >> 3), c = lane & 7;
+      const bool g = __shfl_sync(0xffffffffu, good, rr);
+      if (g) {
+        const uint4 u = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((c ^ (rr & 7)) << 4));
+        *reinterpret_cast<uint4*>(out + (static_cast<size_t>(row_base + rr) * H + h) * D +
+                                  ch * kCols + c * kEl) = u;
+      }
+    }
+    __syncwarp();
+  }
+}
+
 template <typename TO>
 __device__ __forceinline__ void store_row32(TO* dst, const float* v, float scale);
 template <>

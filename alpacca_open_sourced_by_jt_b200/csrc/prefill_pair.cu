@@ -25,7 +25,7 @@
 // producer prefetches the next item's Q and K/V while the current item drains.
 //
 // 384 threads:
-//   warp 0        TMA producer (Q pair, then K_j / V_j into a 5-slot ring)
+//   warp 0        TMA producer (Q pair, then K_j / V_j into a 4-slot ring)
 //   warp 1        TMEM owner, single-lane MMA issuer
 //   warps 2-3     idle
 //   warps 4-7     softmax warpgroup for head h0 (TMEM lanes = query rows)
@@ -35,17 +35,21 @@
 // (128 x 120 + 256 x 192 = 64512, the launch total).  The host
 // refuses to launch if the compiled register count is not 168.
 // TMEM (512 columns): S0/P0 [0,128) S1/P1 [128,256) O0 [256,256+D)
-// O1 [384,384+D).  SMEM (D=128): Q0, Q1 32 KB each, 5 K/V slots of 32 KB.
+// O1 [384,384+D).  SMEM (D=128): Q0, Q1 32 KB each, 4 K/V slots of 32 KB,
+// 8 x 4 KB epilogue staging (one buffer per softmax warp).
 //
 // Ordering facts the pipeline relies on (tcgen05.commit arrives only when
 // every MMA the issuing thread issued before it has completed):
 //   * QK_t(j+1) is issued after PV_t(j), so when S_t(j+1) is ready, PV_t(j)
 //     has read P_t(j) and its columns may be overwritten;
-//   * PV_t(j) is issued only after the softmax released P_t(j); a softmax
-//     that must rescale O_t (rare: its running max grew by more than 2^8)
-//     first waits for PV_t(j-1).  PV g of head t arrives on pv[t][g & 1],
-//     phase g >> 1, so skipped waits never make a parity wait ambiguous
-//     (PV g+2 needs P g+2, which the waiting softmax has not released).
+//   * P_t(j) is released in two halves (keys 0-63 on ph[t], 64-127 on
+//     pf[t]) and PV_t(j) is issued in the same two halves, so the first
+//     half's MMAs overlap the second half's exponentials; a softmax that
+//     must rescale O_t (rare: its running max grew by more than 2^8) does
+//     so before the first release (S_t(j) ready implies PV_t(j-1) done);
+//   * only an item's last PV_t commits pv[t] (one phase per item, waited for
+//     by that item's epilogue; the next phase needs a P the epilogue's
+//     softmax has not released yet, so parity waits stay unambiguous).
 //
 // Positions must be non-decreasing within each 128-token tile (a prefill
 // chunk's positions always are): the key range of a tile is taken from its
@@ -75,7 +79,7 @@ using prefill::tc_wait_ld;
 using prefill::tc_wait_st;
 
 constexpr int kThreads = 384;
-constexpr int kSlots = 5;
+constexpr int kSlots = 4;
 constexpr int kLaunchRegs = 168;
 constexpr int kProducerRegs = 120;
 constexpr int kSoftmaxRegs = 192;
@@ -90,7 +94,8 @@ struct Layout {
   static constexpr int kQ0 = 0;
   static constexpr int kQ1 = kTile;
   static constexpr int kRing = 2 * kTile;
-  static constexpr int kTotal = kRing + kSlots * kTile;
+  static constexpr int kStage = kRing + kSlots * kTile;  // 8 softmax warps x 4 KB
+  static constexpr int kTotal = kStage + 8 * 4096;
   static constexpr int kSmem = kTotal + 1024;
 };
 
@@ -137,7 +142,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_qf, bar_qe;
   __shared__ __align__(8) uint64_t bar_full[kSlots], bar_empty[kSlots];
-  __shared__ __align__(8) uint64_t bar_sf[2], bar_pf[2], bar_pv[2][2], bar_oe[2];
+  __shared__ __align__(8) uint64_t bar_sf[2], bar_ph[2], bar_pf[2], bar_pv[2], bar_oe[2];
   __shared__ uint32_t s_tmem;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -154,9 +159,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bar_sf[t], 1);
+      mbar_init(&bar_ph[t], 4);
       mbar_init(&bar_pf[t], 4);
-      mbar_init(&bar_pv[t][0], 1);
-      mbar_init(&bar_pv[t][1], 1);
+      mbar_init(&bar_pv[t], 1);
       mbar_init(&bar_oe[t], 4);
     }
     fence_mbar_init();
@@ -194,6 +199,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
           tma_load_3d(smem + L::kQ1 + b * L::kBox, &tmQ, &bar_qf, b * 64, it.h0 + 1, it.row0);
         }
         ++qcnt;
+        // the next item's Q tiles and first K/V tiles come from HBM: start
+        // them towards L2 now, an item ahead of their loads
+        {
+          const int nidx = item_index(k + 1, c, G);
+          if (nidx < n_items) {
+            const Item nt = make_item(nidx, pos, n_q, t_kv, H, group, n_q_tiles, window, kv_start);
+#pragma unroll
+            for (int b = 0; b < D / 64; ++b) {
+              tma_prefetch_l2_3d(&tmQ, b * 64, nt.h0, nt.row0);
+              tma_prefetch_l2_3d(&tmQ, b * 64, nt.h0 + 1, nt.row0);
+              for (int j = nt.j0; j < nt.jend && j < nt.j0 + 2; ++j) {
+                tma_prefetch_l2_3d(&tmK, b * 64, nt.kvh, j * kBN);
+                tma_prefetch_l2_3d(&tmV, b * 64, nt.kvh, j * kBN);
+              }
+            }
+          }
+        }
         for (int j = it.j0; ok && j < it.jend; ++j) {
 #pragma unroll
           for (int kv = 0; kv < 2; ++kv) {
@@ -224,7 +246,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
       const uint64_t dV0 = sw128_desc(smem_u32(smem + L::kRing), L::kBox, 1024);
       constexpr uint64_t kSlotStep = L::kTile >> 4;
       uint32_t seq = 0, qcnt = 0, pcnt0 = 0, pcnt1 = 0;
-      uint32_t pvg[2] = {0, 0};  // PVs issued per head (running)
       bool ok = true;
       auto qk = [&](int t, uint32_t kslot) {
         const uint64_t dk = dK0 + kslot * kSlotStep;
@@ -236,15 +257,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
         }
         tc_commit(&bar_sf[t]);
       };
-      auto pv = [&](int t, uint32_t vslot, bool acc) {
+      // PV_t over one half of the key tile (keys 64*half .. 64*half+63);
+      // the item's last PV commits the head's PV barrier (the epilogue's
+      // wait; every earlier PV_t completed before the next S_t was ready)
+      auto pv = [&](int t, uint32_t vslot, bool acc, int half, bool last) {
         const uint64_t dv = dV0 + vslot * kSlotStep;
         const uint32_t tp = tmem + t * kBN;  // P_t: 16 keys per 8 columns
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
+        for (int k4 = 0; k4 < kBN / 32; ++k4) {
+          const int kk = half * (kBN / 32) + k4;
           tc_mma_ts(tmem + 2 * kBN + t * 128, tp + kk * 8, dv + ((kk * 16 * 128) >> 4), idesc_pv,
                     (acc || kk > 0));
-        tc_commit(&bar_pv[t][pvg[t] & 1]);
-        ++pvg[t];
+        }
+        if (half && last) tc_commit(&bar_pv[t]);
       };
       for (int k = 0; ok; ++k) {
         const int idx = item_index(k, c, G);
@@ -273,12 +298,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
             uint32_t& pc = t ? pcnt1 : pcnt0;
-            if (!mbar_wait(&bar_pf[t], pc & 1, 0x15000 | jj)) { ok = false; break; }
-            ++pc;
+            // first half of P_t(jj): its PV runs while the softmax computes
+            // the second half's exponentials
+            if (!mbar_wait(&bar_ph[t], pc & 1, 0x15000 | jj)) { ok = false; break; }
             if (jj == 0 && qcnt > 0 && !mbar_wait(&bar_oe[t], (qcnt - 1) & 1, 0x16000)) { ok = false; break; }
             if (t == 0 && !mbar_wait(&bar_full[vs], (vsq / kSlots) & 1, 0x17000 | jj)) { ok = false; break; }
             tc_fence_after();
-            pv(t, vs, jj > 0);
+            pv(t, vs, jj > 0, 0, false);
+            if (!mbar_wait(&bar_pf[t], pc & 1, 0x15800 | jj)) { ok = false; break; }
+            ++pc;
+            tc_fence_after();
+            pv(t, vs, true, 1, jj + 1 == n);
             if (t == 1) tc_commit(&bar_empty[vs]);
             if (jj + 1 < n) {
               if (t == 0 && !mbar_wait(&bar_full[ks], (ksq / kSlots) & 1, 0x18000 | jj)) { ok = false; break; }
@@ -302,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
     const int r = (warp & 3) * 32 + lane;         // query row within the tile == TMEM lane
     const uint32_t tl = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const uint32_t s_col = t * kBN, o_col = 2 * kBN + t * 128;
-    uint32_t scnt = 0, pvbase = 0;  // pvbase: this head's PVs before the item
+    uint32_t scnt = 0, icnt = 0;  // icnt: items this head has finished
     bool ok = true;
     for (int k = 0; ok; ++k) {
       const int idx = item_index(k, c, G);
@@ -373,62 +403,59 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
         const float mref = (m == -INFINITY) ? 0.f : m;
         // P_t(jj) as 16-bit pairs over the first 64 columns of S_t (the whole
         // score row is in registers; PV_t(jj-1), the last reader of those
-        // columns, completed before QK_t(jj) did), 32 keys per store
+        // columns, completed before QK_t(jj) did), 32 keys per store, in two
+        // halves: the MMA warp starts PV on keys 0-63 while keys 64-127 are
+        // exponentiated
         float suma = 0.f, sumb = 0.f;
 #pragma unroll
-        for (int qtr = 0; qtr < 4; ++qtr) {
-          uint32_t pk[16];
+        for (int half = 0; half < 2; ++half) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float p0 = fast_exp2(fmaf(s[qtr * 32 + 2 * e], sscale, -mref));
-            const float p1 = fast_exp2(fmaf(s[qtr * 32 + 2 * e + 1], sscale, -mref));
-            if (e & 1) sumb += p0 + p1; else suma += p0 + p1;
-            pk[e] = Pack2<T>::run(p0, p1);
+          for (int q2 = 0; q2 < 2; ++q2) {
+            const int qtr = half * 2 + q2;
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float p0 = fast_exp2(fmaf(s[qtr * 32 + 2 * e], sscale, -mref));
+              const float p1 = fast_exp2(fmaf(s[qtr * 32 + 2 * e + 1], sscale, -mref));
+              if (e & 1) sumb += p0 + p1; else suma += p0 + p1;
+              pk[e] = Pack2<T>::run(p0, p1);
+            }
+            tc_st16(tl + s_col + qtr * 16, pk);
           }
-          tc_st16(tl + s_col + qtr * 16, pk);
-        }
-        tc_wait_st();
-        l = l * alpha + (suma + sumb);
-        // only an O rescale needs PV_t(jj-1) complete (PV_t(jj) is issued
-        // after this release, so it cannot race the rescale)
-        if (warp_need && jj > 0) {
-          const uint32_t g = pvbase + jj - 1;
-          ok = __all_sync(0xffffffffu, mbar_wait(&bar_pv[t][g & 1], (g >> 1) & 1, 0x1A000 | jj));
-          if (!ok) break;
-          tc_fence_after();
+          // an O rescale comes before the first release (PV_t(jj) starts on
+          // it), once the first half's scores are dead.  PV_t(jj-1)
+          // completed before QK_t(jj) did (commit order), so O_t is final.
+          if (half == 0 && warp_need && jj > 0) {
 #pragma unroll
-          for (int cc = 0; cc < D / 32; ++cc) {
-            float o[32];
-            tc_ld32(tl + o_col + cc * 32, o);
-            tc_wait_ld();
+            for (int cc = 0; cc < D / 32; ++cc) {
+              float o[32];
+              tc_ld32(tl + o_col + cc * 32, o);
+              tc_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] *= alpha;
-            tc_st32(tl + o_col + cc * 32, o);
+              for (int e = 0; e < 32; ++e) o[e] *= alpha;
+              tc_st32(tl + o_col + cc * 32, o);
+            }
           }
           tc_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(half ? &bar_pf[t] : &bar_ph[t]);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bar_pf[t]);
+        if (!ok) break;
+        l = l * alpha + (suma + sumb);
       }
       if (!ok) break;
       // epilogue: wait for the last PV (every earlier one completed before
       // it), O / l -> out, release O
       {
-        const uint32_t g = pvbase + n - 1;
-        ok = __all_sync(0xffffffffu, mbar_wait(&bar_pv[t][g & 1], (g >> 1) & 1, 0x1B000));
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_pv[t], icnt & 1, 0x1B000));
       }
       if (!ok) break;
-      pvbase += n;
+      ++icnt;
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-#pragma unroll
-      for (int cc = 0; cc < D / 32; ++cc) {
-        float o[32];
-        tc_ld32(tl + o_col + cc * 32, o);
-        tc_wait_ld();
-        if (valid_row && l > 0.f) store_row32<TO>(orow + cc * 32, o, inv);
-      }
+      prefill::store_o_rows<TO, D>(tl + o_col, smem + L::kStage + (warp - 4) * 4096, out,
+                                   it.row0 + (warp & 3) * 32, H, h, inv, valid_row && l > 0.f);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_oe[t]);
