@@ -20,7 +20,7 @@
 // The grid is persistent (at most one CTA per SM): CTA c takes items c,
 // 2G-1-c, 2G+c, ... of the heaviest-first item list (snake order); the
 // producer loads the next item's Q as soon as the current item's last QK
-// has completed, and keeps streaming K/V tiles through a 4-slot ring.
+// has completed, and keeps streaming K/V tiles through a ring of K/V slots.
 //
 // 256 threads: warp 0 TMA producer, warp 1 TMEM owner + single-lane MMA
 // issuer, warps 2-3 idle, warps 4-7 softmax (thread = query row = TMEM lane).
@@ -28,7 +28,8 @@
 // where a 128-key K or V tile (64 KB) would leave room for only one ring slot.
 // TMEM (512 columns): S0/P0 [0,BN), S1/P1 [BN,2BN), O [2BN, 2BN+D) (for
 // D = 256: 64 + 64 + 256 columns).  SMEM: Q (128 x D), then a ring of K/V
-// slots of BN x D: 6 slots of 32 KB for D = 128, 5 of 32 KB for D = 256.
+// slots of BN x D: 5 slots of 32 KB for D = 128, 4 of 32 KB for D = 256,
+// then 4 x 4 KB epilogue staging (one buffer per softmax warp).
 //
 // Barrier phases use running counters; where one side may run two steps
 // ahead, two barriers alternate (index g & 1, phase g >> 1) so that every
@@ -52,7 +53,6 @@ using prefill::kLog2e;
 using prefill::kRescaleThreshold;
 using prefill::Pack2;
 using prefill::make_idesc;
-using prefill::store_row32;
 using prefill::sw128_desc;
 using prefill::tc_commit;
 using prefill::tc_fence_after;
@@ -75,14 +75,15 @@ struct KeyTile {
 
 template <int D, int BN>
 struct Layout {
-  static constexpr int kSlots = D > 128 ? 5 : 6;
+  static constexpr int kSlots = D > 128 ? 4 : 5;
   static constexpr int kBoxQ = 128 * 128;            // 128 query rows x 128 B
   static constexpr int kBoxKV = BN * 128;            // BN key rows x 128 B
   static constexpr int kTileQ = (D / 64) * kBoxQ;    // Q tile (128 rows x D)
   static constexpr int kTileKV = (D / 64) * kBoxKV;  // K or V tile (BN rows x D)
   static constexpr int kQ = 0;
   static constexpr int kRing = kTileQ;
-  static constexpr int kTotal = kRing + kSlots * kTileKV;
+  static constexpr int kStage = kRing + kSlots * kTileKV;  // 4 softmax warps x 4 KB
+  static constexpr int kTotal = kStage + 4 * 4096;
   static constexpr int kSmem = kTotal + 1024;
   static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
   static_assert(2 * BN + D <= 512, "S double buffer + O must fit in 512 TMEM columns");
@@ -399,13 +400,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_head_kernel(
       pvbase += n;
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-#pragma unroll
-      for (int cc = 0; cc < D / 32; ++cc) {
-        float o[32];
-        tc_ld32(tl + o_col + cc * 32, o);
-        tc_wait_ld();
-        if (valid_row && l > 0.f) store_row32<TO>(orow + cc * 32, o, inv);
-      }
+      prefill::store_o_rows<TO, D>(tl + o_col, smem + L::kStage + (warp - 4) * 4096, out,
+                                   it.row0 + (warp & 3) * 32, H, it.h, inv, valid_row && l > 0.f);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_oe);

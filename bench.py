@@ -721,10 +721,10 @@ def bench_e2e(dev, st, steps, warmup, dist=None):
                      "D2H), host waits for each step")
 
 
-def bench_prefill(dev, steps, warmup):
+def bench_prefill(dev, steps, warmup, shape=None):
     import torch
     from alpacca_open_sourced_by_jt_b200 import device
-    S, H, KV, D = PF["S"], PF["H"], PF["KV"], PF["D"]
+    S, H, KV, D = shape or (PF["S"], PF["H"], PF["KV"], PF["D"])
     g = torch.Generator(device=dev).manual_seed(1)
     q = torch.randn((S, H, D), device=dev, dtype=torch.bfloat16, generator=g)
     k = torch.randn((S, KV, D), device=dev, dtype=torch.bfloat16, generator=g)
@@ -857,9 +857,11 @@ def run_ours(args):
         # slowest rank's step time counts for all
         e2e = bench_e2e(dev, st, args.steps, args.warmup, dist)
     if rank == 0:
-        pf = None
+        pf = pf256 = None
         if args.only in (None, "prefill") and not args.no_prefill:
             pf = bench_prefill(dev, args.steps, args.warmup)
+            # head_dim 256 (the Qwen35 full-attention geometry: 16 q / 2 KV heads)
+            pf256 = bench_prefill(dev, args.steps, args.warmup, shape=(PF["S"], 16, 2, 256))
         _lib.raise_device_error()
         cpu = cpu_decode_baseline(st) if (world == 1 and not args.no_cpu_baseline) else None
         traffic = profiled_traffic("decode_mma_kernel bf16 D128 NT1")
@@ -921,6 +923,16 @@ def run_ours(args):
                                        "GQA groups)",
                              "peak_source": f"{src} (MEASURED_PEAKS.json bf16_tflops, burst)"},
                 "launches": pf["launches"]}
+            if pf256:
+                result["prefill"]["head_dim_256"] = {
+                    "value": round(pf256["tflops"], 1), "unit": "TFLOP/s",
+                    "ms_per_launch": round(pf256["ms"], 4),
+                    "config": f"S={PF['S']} causal, 16 q / 2 KV heads, D=256, bf16 in/out, "
+                              "fp32 accumulation (Qwen35 full-attention layers); L2 flushed",
+                    "kernel": "prefill_head_kernel<bf16,bf16,256> (64-key tiles)",
+                    "roofline": {"bound": "tensor", "achieved": round(pf256["tflops"], 1),
+                                 "peak": bf16, "unit": "TFLOP/s",
+                                 "frac": round(pf256["tflops"] / bf16, 4)}}
             if pcpu:
                 result["prefill"]["cpu_baseline"] = pcpu
     if dist is not None:
