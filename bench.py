@@ -98,16 +98,19 @@ def peaks():
         return FALLBACK_HBM, FALLBACK_BF16, 1400.0, "fallback"
 
 
+# Per-launch DRAM traffic, dram__bytes_read.sum + dram__bytes_write.sum, from the ncu
+# captures summarised in profiles/decode_mma_bf16_32k.md (2 sequences, scaled x8 to the
+# 16-sequence launch: reads scale with the rows) and profiles/prefill_pair_bf16_s2048.md
+# (one full config-2 launch).
+NCU_TRAFFIC = {
+    "decode_mma_kernel bf16 D128 NT1": 2179069952.0,
+    "prefill_pair_kernel bf16 D128": 25243392.0,
+}
+
+
 def profiled_traffic(name):
-    """Per-launch DRAM traffic recorded from an ncu capture in profiles/."""
-    p = os.path.join(REPO, "profiles", "traffic.md")
-    try:
-        for line in open(p):
-            if line.startswith(f"| {name} |"):
-                return float(line.split("|")[2].strip())
-    except OSError:
-        pass
-    return None
+    """Per-launch DRAM traffic of `name` from an ncu capture (None if not captured)."""
+    return NCU_TRAFFIC.get(name)
 
 
 # ---------------------------------------------------------------------------
