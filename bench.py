@@ -321,10 +321,11 @@ def bench_varlen(dev, rank, world, steps, warmup, dist):
     sequences r, r + N, ...; no collective).  One step is the device half of
     a batched decode token: the fused RoPE + append kernel rotates every
     sequence's new q/k row at position L_b and stores k/v there, then the
-    split-KV decode (split + combine kernels) attends over L_b + 1 rows.
-    Bytes per step: the KV rows read, sum_b 2*(L_b+1)*KV*D*2, plus the new
-    rows and q/out traffic, over the whole batch; the time is the max over
-    ranks (strong scaling)."""
+    split-KV decode (split + combine kernels) attends over L_b + 1 rows; the
+    step is captured once and replayed as a CUDA graph.  Bytes per step: the
+    KV rows read, sum_b 2*(L_b+1)*KV*D*2, plus the new rows and q/out
+    traffic, over the whole batch; the time is the max over ranks (strong
+    scaling)."""
     import numpy as np
     import torch
     from alpacca_open_sourced_by_jt_b200 import device
@@ -352,8 +353,20 @@ def bench_varlen(dev, rank, world, steps, warmup, dist):
                            q_out=qr)
         device.decode(qr, kc, vc, lens, out=out, workspace=ws, split_rows=split, max_len=n_ctx)
 
+    # the step replayed as one CUDA graph, as a serving loop runs it (positions and
+    # lengths are read on the device): at 8 sequences per GPU the three eager launches'
+    # host cost would otherwise set the pace
+    step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            step()
+    torch.cuda.current_stream().wait_stream(side)
     for _ in range(max(warmup, 3)):
-        step()
+        graph.replay()
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
@@ -362,7 +375,7 @@ def bench_varlen(dev, rank, world, steps, warmup, dist):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(nsteps):
-        step()
+        graph.replay()
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
@@ -375,6 +388,7 @@ def bench_varlen(dev, rank, world, steps, warmup, dist):
     extra = Bt * 2 * KV * D * (4 + 2) + Bt * H * D * 4 * 4  # new rows in/out; q, q_rot x2, out
     per_step = kv_bytes + extra
     local = int(sum(2 * (int(L) + 1) * KV * D * 2 for L in Ls)) + extra * B // Bt
+    del graph
     del kc, vc
     return {"metric": "varlen batched decode GB/s (config 3)",
             "value": round(per_step / (ms / nsteps * 1e-3) / 1e9, 1), "unit": "GB/s",
@@ -384,8 +398,9 @@ def bench_varlen(dev, rank, world, steps, warmup, dist):
             "achieved_per_gpu_max": round(local / (ms / nsteps * 1e-3) / 1e9, 1),
             "config": "one batch of 64 seqs sharded by sequence over the GPUs, L_b ~ "
                       f"U[1024,8192] (seed 2; mean {float(Ls_all.mean()):.0f}), 32 q / 8 KV "
-                      "heads, D=128, fp16 KV; per step: fused RoPE+append of each new token "
-                      "at L_b, split-KV decode over L_b+1 rows; KV bytes > L2, no flush"}
+                      "heads, D=128, fp16 KV; per step (one CUDA graph): fused RoPE+append "
+                      "of each new token at L_b, split-KV decode over L_b+1 rows; KV bytes > "
+                      "L2, no flush"}
 
 
 def bench_kvstate(dev, steps, warmup):
