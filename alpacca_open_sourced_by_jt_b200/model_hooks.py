@@ -13,8 +13,10 @@ versions with the same signatures:
 They read the model's own hyperparameters and its f32 cos/sin tables
 (model.py:871-875), so rotations are bit-identical and attention matches to
 the tolerances of `kernels.attention_decode` / `cuda.attention_batch`.
-Nothing else in the model changes; `uninstall(model)` restores the
-class methods.
+A prefill shape no kernel serves (head_dim not a multiple of 4, or above
+256) is declined as the reference's GPU tier declines it (cuda.py:1219-1222),
+and the model's own class method answers.  Nothing else in the model
+changes; `uninstall(model)` restores the class methods.
 """
 from __future__ import annotations
 
@@ -40,8 +42,10 @@ def _attention_np(self, q, K, V, group: int, inv_sqrt: float):
 def _attention_batch_np(self, q, K, V, positions, group: int, inv_sqrt: float):
     out = _cuda.attention_batch(q, K, V, positions, group, inv_sqrt)
     if out is None:
-        raise ValueError(f"B200 prefill does not serve head_dim {self.hp.head_dim} "
-                         "(a multiple of 4 up to 256); no CPU fallback is installed")
+        # cuda.attention_batch declined the shape (head_dim not a multiple of 4
+        # or above 256), exactly as the reference's GPU tier declines: the
+        # model keeps its own, unhooked method (model.py:1254-1272)
+        return type(self)._attention_batch_np(self, q, K, V, positions, group, inv_sqrt)
     return out
 
 
@@ -49,8 +53,9 @@ def _attention_batch_window_np(self, q, K, V, positions, group: int, inv_sqrt: f
                                window: int = 0, kv_start: int = 0):
     out = _cuda.attention_batch(q, K, V, positions, group, inv_sqrt, window, kv_start)
     if out is None:
-        raise ValueError(f"B200 prefill does not serve head_dim {self.hp.head_dim} "
-                         "(a multiple of 4 up to 256); no CPU fallback is installed")
+        # declined shape: the model's own method (model.py:1567-1592)
+        return type(self)._attention_batch_window_np(self, q, K, V, positions, group, inv_sqrt,
+                                                     window, kv_start)
     return out
 
 

@@ -120,10 +120,18 @@ def test_prefill_hooks_including_head_dim_256(cuda_dev, golden):
                                           d["H"] // d["KV"], 1.0 / math.sqrt(d["D"]),
                                           d["window"], d["kv_start"])
     assert rel_err(out, gm["window_d256"]) < 1e-4
-    # a head_dim no kernel serves raises (no silent CPU fallback is installed)
+    # a head_dim no kernel serves (6: not a multiple of 4) is declined by
+    # cuda.attention_batch, as the reference's GPU tier declines, and the
+    # model's own (class) method answers, as it does in the reference
     m6 = StandInModel(2, 1, 6, 6, 10000.0, "norm", 8)
     model_hooks.install(m6)
-    with pytest.raises(ValueError):
-        m6._attention_batch_np(np.zeros((2, 2, 6), np.float32), np.zeros((2, 1, 6), np.float32),
-                               np.zeros((2, 1, 6), np.float32), np.array([0, 1], np.int32), 2,
-                               0.4)
+    rng = np.random.default_rng(6)
+    args = (rng.standard_normal((2, 2, 6)).astype(np.float32),
+            rng.standard_normal((2, 1, 6)).astype(np.float32),
+            rng.standard_normal((2, 1, 6)).astype(np.float32), np.array([0, 1], np.int32), 2, 0.4)
+    from alpacca_open_sourced_by_jt_b200 import cuda as b200_cuda
+    assert b200_cuda.attention_batch(*args) is None
+    got = m6._attention_batch_np(*args)
+    assert np.array_equal(got, StandInModel._attention_batch_np(m6, *args))
+    gotw = m6._attention_batch_window_np(*args, 1, 0)
+    assert np.array_equal(gotw, StandInModel._attention_batch_window_np(m6, *args, 1, 0))
