@@ -90,8 +90,70 @@ __device__ __noinline__ void publish_group(const shard::Publish pub, const float
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32));
   if (!s_last) return;
   __threadfence();
+  constexpr int kT = kConsumerWarps * 32;
   const int r0 = b * H + kvh * group;
-  for (int idx = threadIdx.x; idx < group * (D + 1); idx += kConsumerWarps * 32) {
+  // The merge runs at the tail of the kernel on one CTA per group, so it is
+  // latency-bound: every split's (m, l) of the group is loaded at once into
+  // shared memory, each head's weights w = 2^(m - M) / L are formed once,
+  // and each value then needs one batch of independent loads.
+  constexpr int kMaxW = 1024;  // group x splits weights held in shared memory
+  __shared__ float s_w[kMaxW];
+  __shared__ float s_lse[32];
+  __shared__ uint32_t s_steps[32];
+  const bool fits = group * ns_b <= kMaxW && group <= 32;
+  if (fits) {
+    for (int i = threadIdx.x; i < group * ns_b; i += kT) {
+      const int n = i / ns_b, sp = i - n * ns_b;
+      s_w[i] = __ldcg(part_ml + (static_cast<size_t>(r0 + n) * n_splits + sp) * 2);
+    }
+    if (threadIdx.x < group) s_steps[threadIdx.x] = __ldcg(steps + r0 + threadIdx.x);
+    asm volatile("bar.sync 1, %0;" ::"n"(kT));
+    for (int n = threadIdx.x; n < group; n += kT) {
+      const size_t p0 = static_cast<size_t>(r0 + n) * n_splits;
+      float M = -INFINITY;
+      for (int sp = 0; sp < ns_b; ++sp) M = fmaxf(M, s_w[n * ns_b + sp]);
+      const float Mref = (M == -INFINITY) ? 0.f : M;
+      float L = 0.f;
+      for (int sp = 0; sp < ns_b; ++sp) {
+        const float w = exp2f(s_w[n * ns_b + sp] - Mref);
+        L += __ldcg(part_ml + (p0 + sp) * 2 + 1) * w;
+        s_w[n * ns_b + sp] = w;
+      }
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      for (int sp = 0; sp < ns_b; ++sp) s_w[n * ns_b + sp] *= inv;
+      s_lse[n] = L > 0.f ? (Mref + log2f(L)) * 0.6931471805599453f : -INFINITY;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kT));
+    for (int idx = threadIdx.x; idx < group * (D + 1); idx += kT) {
+      const int n = idx / (D + 1), d = idx - n * (D + 1);
+      float val;
+      if (d < D) {
+        const float* po = part_o + static_cast<size_t>(r0 + n) * n_splits * D + d;
+        const float* w = s_w + n * ns_b;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int sp = 0;
+        for (; sp + 3 < ns_b; sp += 4) {
+          a0 += __ldcg(po + static_cast<size_t>(sp) * D) * w[sp];
+          a1 += __ldcg(po + static_cast<size_t>(sp + 1) * D) * w[sp + 1];
+          a2 += __ldcg(po + static_cast<size_t>(sp + 2) * D) * w[sp + 2];
+          a3 += __ldcg(po + static_cast<size_t>(sp + 3) * D) * w[sp + 3];
+        }
+        for (; sp < ns_b; ++sp) a0 += __ldcg(po + static_cast<size_t>(sp) * D) * w[sp];
+        val = (a0 + a1) + (a2 + a3);
+      } else {
+        val = s_lse[n];
+      }
+      const int r = r0 + n;
+      const uint32_t step = s_steps[n];
+      for (int g = 0; g < pub.G; ++g) {
+        uint2* dst = reinterpret_cast<uint2*>(pub.peers[g] + xl.words) +
+                     shard::word_index(static_cast<int>(step & 1u), pub.me, r, R, pub.G, D);
+        shard::st_tagged(dst + d, val, step + 1u);
+      }
+    }
+    return;
+  }
+  for (int idx = threadIdx.x; idx < group * (D + 1); idx += kT) {
     const int n = idx / (D + 1), d = idx - n * (D + 1);
     const size_t p0 = static_cast<size_t>(r0 + n) * n_splits;
     float M = -INFINITY;

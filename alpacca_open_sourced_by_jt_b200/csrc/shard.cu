@@ -168,26 +168,42 @@ __global__ void __launch_bounds__(kThreads) shard_exchange_kernel(
   // phase B: every rank's part of each row, then the merge
   const uint64_t t_end = globaltimer_ns() + kShardWaitNs;
   bool hit = false;  // this thread's waits ran out: it stops waiting
+  // Latency-bound: the G lse words of a row are waited for by G threads at
+  // once and shared; each value thread then issues its G loads in batches
+  // of 8 before it checks their tags (and spins only on a late one).
+  __shared__ float s_gl[kThreads];  // each rank's lse of the current row (G <= kThreads)
   for (int r = blockIdx.x; r < R; r += gridDim.x) {
     const uint32_t step = steps[r];
     const uint32_t tag = step + 1u;
     const int parity = static_cast<int>(step & 1u);
+    if (threadIdx.x < G)
+      s_gl[threadIdx.x] =
+          wait_tagged(words + word_index(parity, threadIdx.x, r, R, G, D) + D, tag, t_end, &hit);
+    __syncthreads();
     float M = -INFINITY;
-    for (int g = 0; g < G; ++g)
-      M = fmaxf(M, wait_tagged(words + word_index(parity, g, r, R, G, D) + D, tag, t_end, &hit));
+    for (int g = 0; g < G; ++g) M = fmaxf(M, s_gl[g]);
     const float Mref = (M == -INFINITY) ? 0.f : M;
     float L = 0.f;
-    for (int g = 0; g < G; ++g) {
-      const float l = __uint_as_float(ld_tagged(words + word_index(parity, g, r, R, G, D) + D).x);
-      L += expf(l - Mref);
-    }
+    for (int g = 0; g < G; ++g) L += expf(s_gl[g] - Mref);
     const float invL = (L > 0.f) ? 1.f / L : 0.f;
     for (int d = threadIdx.x; d < D; d += kThreads) {
       float acc = 0.f;
-      for (int g = 0; g < G; ++g) {
-        const uint2* src = words + word_index(parity, g, r, R, G, D);
-        const float w = expf(__uint_as_float(ld_tagged(src + D).x) - Mref);
-        acc += w * wait_tagged(src + d, tag, t_end, &hit);
+      for (int g0 = 0; g0 < G; g0 += 8) {
+        const int gn = min(8, G - g0);
+        uint2 w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (i < gn) w[i] = ld_tagged(words + word_index(parity, g0 + i, r, R, G, D) + d);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (i < gn) {
+            const float v = (w[i].y == tag) ? __uint_as_float(w[i].x)
+                                            : wait_tagged(words + word_index(parity, g0 + i, r, R,
+                                                                             G, D) + d,
+                                                          tag, t_end, &hit);
+            acc += expf(s_gl[g0 + i] - Mref) * v;
+          }
+        }
       }
       out[static_cast<size_t>(r) * D + d] = acc * invL;
     }
