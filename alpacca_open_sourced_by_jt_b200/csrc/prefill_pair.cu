@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
     int n_q_tiles, int n_items, float sscale, int window, int kv_start) {
   using L = Layout<D>;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bar_qf, bar_qe;
+  __shared__ __align__(8) uint64_t bar_qf[2], bar_qe;
   __shared__ __align__(8) uint64_t bar_full[kSlots], bar_empty[kSlots];
   __shared__ __align__(8) uint64_t bar_sf[2], bar_ph[2], bar_pf[2], bar_pv[2], bar_oe[2];
   __shared__ uint32_t s_tmem;
@@ -151,7 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
   const int c = blockIdx.x, G = gridDim.x;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bar_qf, 1);
+    mbar_init(&bar_qf[0], 1);
+    mbar_init(&bar_qf[1], 1);
     mbar_init(&bar_qe, 1);
     for (int s = 0; s < kSlots; ++s) {
       mbar_init(&bar_full[s], 1);
@@ -192,12 +193,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
         const Item it = make_item(idx, pos, n_q, t_kv, H, group, n_q_tiles, window, kv_start);
         if (it.jend - it.j0 <= 0) continue;
         if (qcnt > 0 && !mbar_wait(&bar_qe, (qcnt - 1) & 1, 0x11000 | k)) break;
-        mbar_arrive_expect_tx(&bar_qf, 2 * L::kTile);
+        // Q of the first head, then (in the ring loop) the first K tile, then
+        // Q of the second head: QK of the first head starts after 64 KB
+        // instead of 96 KB (at a cold start every byte comes from HBM)
+        mbar_arrive_expect_tx(&bar_qf[0], L::kTile);
 #pragma unroll
-        for (int b = 0; b < D / 64; ++b) {
-          tma_load_3d(smem + L::kQ0 + b * L::kBox, &tmQ, &bar_qf, b * 64, it.h0, it.row0);
-          tma_load_3d(smem + L::kQ1 + b * L::kBox, &tmQ, &bar_qf, b * 64, it.h0 + 1, it.row0);
-        }
+        for (int b = 0; b < D / 64; ++b)
+          tma_load_3d(smem + L::kQ0 + b * L::kBox, &tmQ, &bar_qf[0], b * 64, it.h0, it.row0);
         ++qcnt;
         // the next item's Q tiles and first K/V tiles come from HBM: start
         // them towards L2 now, an item ahead of their loads
@@ -231,6 +233,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
               tma_load_3d(dst + b * L::kBox, kv ? &tmV : &tmK, &bar_full[slot], b * 64, it.kvh,
                           j * kBN);
             ++seq;
+            if (j == it.j0 && kv == 0) {
+              mbar_arrive_expect_tx(&bar_qf[1], L::kTile);
+#pragma unroll
+              for (int b = 0; b < D / 64; ++b)
+                tma_load_3d(smem + L::kQ1 + b * L::kBox, &tmQ, &bar_qf[1], b * 64, it.h0 + 1,
+                            it.row0);
+            }
           }
         }
       }
@@ -277,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
         const Item it = make_item(idx, pos, n_q, t_kv, H, group, n_q_tiles, window, kv_start);
         const int n = it.jend - it.j0;
         if (n <= 0) continue;
-        if (!mbar_wait(&bar_qf, qcnt & 1, 0x13000 | k)) break;
+        if (!mbar_wait(&bar_qf[0], qcnt & 1, 0x13000 | k)) break;
         const uint32_t base = seq;
         seq += 2 * n;
         // first key tile for both heads
@@ -286,6 +295,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(
           if (!mbar_wait(&bar_full[ks], (base / kSlots) & 1, 0x14000)) break;
           tc_fence_after();
           qk(0, ks);
+          if (!mbar_wait(&bar_qf[1], qcnt & 1, 0x13800 | k)) break;
+          tc_fence_after();
           qk(1, ks);
           tc_commit(&bar_empty[ks]);
           if (n == 1) tc_commit(&bar_qe);
