@@ -103,6 +103,45 @@ struct QkvRope {
   int tab_rows, n_ctx, H, KV, D;
 };
 
+// The CTA's work as segments (tile, first K-block, end K-block).  Tiles
+// (SK false): whole tiles t = c, c + G, ...  Stream-K (SK true): the
+// tiles x K-blocks iterations split evenly over the grid, so every CTA does
+// the same number of MMA K-blocks whatever the tile count; a tile whose
+// K range spans CTAs is summed by their epilogues' atomic adds.  Every role
+// walks the same segments in the same order.
+template <bool SK>
+struct Work {
+  int t, G, n_tiles, nk;
+  long long g, g1;
+  __device__ Work(int c, int G_, int n_tiles_, int nk_) : t(c), G(G_), n_tiles(n_tiles_), nk(nk_) {
+    const long long total = static_cast<long long>(n_tiles_) * nk_;
+    g = total * c / G_;
+    g1 = total * (c + 1) / G_;
+  }
+  __device__ bool next(int& tile, int& kb0, int& kb1) {
+    if (SK) {
+      if (g >= g1) return false;
+      tile = static_cast<int>(g / nk);
+      kb0 = static_cast<int>(g - static_cast<long long>(tile) * nk);
+      kb1 = static_cast<int>(min(static_cast<long long>(nk), kb0 + (g1 - g)));
+      g += kb1 - kb0;
+      return true;
+    }
+    if (t >= n_tiles) return false;
+    tile = t;
+    kb0 = 0;
+    kb1 = nk;
+    t += G;
+    return true;
+  }
+};
+
+__device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+
 template <typename T, typename TO, int Epi, int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
     const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
@@ -110,6 +149,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
     int N, int K, const QkvRope rp) {
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256 && (Epi != 1 || BN == 256),
                 "tile width: 64..256 columns, 256 for the SwiGLU halves");
+  static_assert(Epi != 3 || std::is_same<TO, float>::value, "stream-K adds into an f32 out");
+  constexpr bool kSK = Epi == 3;
   constexpr int kStage = kABytes + BN * kBK * 2;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_full[kStages], bar_empty[kStages];
@@ -155,9 +196,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
       tma_prefetch_desc(&tmW);
       uint32_t it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x) {
+      Work<kSK> wk(blockIdx.x, gridDim.x, n_tiles, nk);
+      int t, kb0, kb1;
+      while (ok && wk.next(t, kb0, kb1)) {
         const int m0 = (t % mt) * kBM, n0 = (t / mt) * BN;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kStages;
           if (it >= kStages &&
               !mbar_wait(&bar_empty[s], ((it / kStages) & 1) ^ 1, 0x31000 | (kb & 0xfff))) {
@@ -190,7 +233,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
       constexpr uint64_t kStageStep = kStage >> 4;
       uint32_t it = 0, tc = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++tc) {
+      Work<kSK> wk(blockIdx.x, gridDim.x, n_tiles, nk);
+      int t, kb0, kb1;
+      for (; ok && wk.next(t, kb0, kb1); ++tc) {
         const uint32_t b = tc & 1;
         // the epilogue has drained this accumulator (two tiles ago)
         if (tc >= 2 && !mbar_wait(&bar_acc_empty[b], ((tc >> 1) - 1) & 1, 0x32000 | (tc & 0xfff))) {
@@ -199,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
         }
         tc_fence_after();
         const uint32_t acc = tmem + b * kAccStride;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kStages;
           if (!mbar_wait(&bar_full[s], (it / kStages) & 1, 0x33000 | (kb & 0xfff))) {
             ok = false;
@@ -209,7 +254,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
           const uint64_t da = dA0 + s * kStageStep, dw = dW0 + s * kStageStep;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)  // 32 bytes of K per MMA inside the swizzle atom
-            tc_mma(acc, da + ((kk * 32) >> 4), dw + ((kk * 32) >> 4), idesc, (kb | kk) != 0);
+            tc_mma(acc, da + ((kk * 32) >> 4), dw + ((kk * 32) >> 4), idesc,
+                   (kb != kb0 || kk != 0) ? 1u : 0u);
           tc_commit(&bar_empty[s]);
         }
         if (ok) tc_commit(&bar_acc_full[b]);
@@ -220,7 +266,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
     const int q = warp & 3;
     const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
     uint32_t tc = 0;
-    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tc) {
+    Work<kSK> wk(blockIdx.x, gridDim.x, n_tiles, nk);
+    int t, kb0, kb1;
+    for (; wk.next(t, kb0, kb1); ++tc) {
       const uint32_t b = tc & 1;
       const bool w = __all_sync(0xffffffffu,
                                 mbar_wait(&bar_acc_full[b], (tc >> 1) & 1, 0x34000 | (tc & 0xfff)));
@@ -276,6 +324,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(
           }
 #pragma unroll
           for (int i = 0; i < 8; ++i) rc[i] = rn[i];
+        }
+      } else if (Epi == 3) {
+        // stream-K: this segment's partial sum is added into out (which
+        // already holds the residual); the tile's other segments add theirs
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tc_ld32(acc + c * 32, v);
+          tc_wait_ld();
+          const int col = n0 + c * 32;
+          if (rv && col < N) {
+            float* dst = reinterpret_cast<float*>(out) + static_cast<size_t>(row) * ldo + col;
+            if (col + 32 <= N) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                red_add_v4(dst + 4 * i, v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (col + i < N) atomicAdd(dst + i, v[i]);
+            }
+          }
         }
       } else if (Epi == 2) {
         // RoPE (norm style, pairs 2i, 2i+1 of a head: adjacent columns of this
@@ -398,7 +468,11 @@ int launch_gemm(const void* a, long long lda, const void* w, long long ldw, cons
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int tiles = ((M + G::kBM - 1) / G::kBM) * ((N + BN - 1) / BN);
-  const int grid = tiles < sms ? tiles : sms;
+  int grid = tiles < sms ? tiles : sms;
+  if (Epi == 3) {  // stream-K: every SM, each with at least one K-block
+    const long long iters = static_cast<long long>(tiles) * ((K + G::kBK - 1) / G::kBK);
+    grid = iters < sms ? static_cast<int>(iters) : sms;
+  }
   e = b2a_host::launch(kern, dim3(grid), dim3(G::kThreads), smem_bytes, st, ta, tw, c_in, ldc,
                        static_cast<TO*>(out), ldo, M, N, K, rp);
   if (e != cudaSuccess) return b2a_host::cuda_fail(e, "gemm launch");
@@ -419,11 +493,27 @@ bool narrow_tiles(int M, int N) {
   return cost(192) < cost(256);
 }
 
+// Stream-K for an in-place f32 residual GEMM (out += a . w^T) whose tiles
+// leave SMs idle: at most two waves of 128 x 256 tiles that do not fill the
+// last one (the chunk's Wo and down projections: 128 tiles on 148 SMs).
+bool use_stream_k(int M, int N) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long tiles = static_cast<long long>((M + 127) / 128) * ((N + 255) / 256);
+  return tiles < 2LL * sms && tiles % sms != 0;
+}
+
 template <typename T, typename TO, int Epi>
 int launch_gemm_auto(const void* a, long long lda, const void* w, long long ldw,
                      const float* c_in, long long ldc, void* out, long long ldo, int M, int N,
                      int K, cudaStream_t st,
                      const b2a::gemm::QkvRope& rp = b2a::gemm::QkvRope{}) {
+  if constexpr (Epi == 0 && std::is_same<TO, float>::value) {
+    if (c_in != nullptr && static_cast<const void*>(c_in) == out && ldc == ldo &&
+        use_stream_k(M, N))
+      return launch_gemm<T, float, 3, 256>(a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st, rp);
+  }
   if (Epi != 1 && narrow_tiles(M, N))
     return launch_gemm<T, TO, Epi, (Epi == 1 ? 256 : 192)>(a, lda, w, ldw, c_in, ldc, out, ldo, M,
                                                            N, K, st, rp);

@@ -72,10 +72,15 @@ def test_gemm_16bit_out_and_strides(cuda_dev, out_dtype, tol):
     assert not out_big[:, N:].any()
 
 
-def test_gemm_residual_in_place(cuda_dev):
+@pytest.mark.parametrize("M,N,K", [(400, 2048, 2048), (2048, 2048, 8192), (130, 200, 520),
+                                   (2048, 2048, 2048)])
+def test_gemm_residual_in_place(cuda_dev, M, N, K):
+    """x += a . w^T in place.  These shapes take the stream-K schedule (fewer
+    than two full waves of tiles): K ranges split across CTAs, each adding
+    its partial sum into x; (130, 200, 520) has a ragged tile edge and a
+    ragged last K block."""
     from alpacca_open_sourced_by_jt_b200 import device
     g = torch.Generator(device=cuda_dev).manual_seed(6)
-    M, N, K = 400, 2048, 2048
     a = torch.randn((M, K), device=cuda_dev, generator=g).to(torch.bfloat16)
     w = (0.02 * torch.randn((N, K), device=cuda_dev, generator=g)).to(torch.bfloat16)
     x = torch.randn((M, N), device=cuda_dev, generator=g)
