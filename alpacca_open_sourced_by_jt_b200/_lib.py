@@ -50,6 +50,7 @@ SIGNATURES = [
     ("b2a_last_error", c_char_p, []),
     ("b2a_device_error", c_int, [POINTER(c_int), POINTER(c_int), c_int]),
     ("b2a_set_launch_flags", c_int, [c_int]),
+    ("b2a_selftest_wait_timeout", c_int, [c_void_p]),
     ("b2a_decode_workspace_bytes", c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     ("b2a_decode_split_rows", c_int, [c_int, c_int, c_int, c_int]),
     ("b2a_decode", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

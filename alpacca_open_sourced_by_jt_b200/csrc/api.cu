@@ -129,3 +129,25 @@ int b2a_device_error(int* code, int* aux, int clear) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Self-test of the bounded mbarrier wait every kernel here uses: one thread
+// initialises a barrier that nothing arrives on and waits for its first
+// phase.  The wait gives up after kWaitLimitNs, records B2A_ERR_TIMEOUT with
+// aux 0x7F000 and the kernel returns normally, so the context stays usable.
+// ---------------------------------------------------------------------------
+namespace b2a {
+__global__ void wait_selftest_kernel() {
+  __shared__ __align__(8) uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  mbar_wait(&bar, 0, 0x7F000);  // no arrival: runs out, records the timeout
+}
+}  // namespace b2a
+
+extern "C" int b2a_selftest_wait_timeout(void* stream) {
+  b2a::wait_selftest_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>();
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return b2a_host::cuda_fail(e, "wait self-test launch");
+  return B2A_OK;
+}

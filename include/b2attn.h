@@ -68,6 +68,13 @@ const char* b2a_last_error(void);
  * device.  Synchronises the device.  *code = 0 means no kernel reported. */
 int b2a_device_error(int* code, int* aux, int clear);
 
+/* No reference counterpart: a self-test of the bounded device waits.  Launches
+ * one thread that waits on an mbarrier nothing arrives on; after the library's
+ * wait limit (2 s) the wait records B2A_ERR_TIMEOUT (aux 0x7F000) and the
+ * kernel returns, leaving the context usable.  Read the record with
+ * b2a_device_error. */
+int b2a_selftest_wait_timeout(void* stream);
+
 /* Launch mode of the calling thread's later launches; returns the previous
  * flags.  B2A_LAUNCH_PDL launches b2a_rope_append, b2a_imrope_append,
  * b2a_decode (both kernels), b2a_lse_combine, b2a_gemm and b2a_gemm_qkv_rope as
