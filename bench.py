@@ -317,8 +317,8 @@ def bench_longctx(dev, rank, world, steps, warmup, dist):
 def bench_varlen(dev, rank, world, steps, warmup, dist):
     """one batch of 64 sequences with cached lengths
     L_b ~ U[1024, 8192] (seed 2), 32 q / 8 KV heads, D=128, fp16 KV ~ N(0,1)
-    (seed 2 + rank), sharded by sequence over the GPUs (rank r holds
-    sequences r, r + N, ...; no collective).  One step is the device half of
+    (seed 2 + rank), sharded by sequence over the GPUs (longctx.place_sequences:
+    longest first onto the rank with the fewest rows; no collective).  One step is the device half of
     a batched decode token: the fused RoPE + append kernel rotates every
     sequence's new q/k row at position L_b and stores k/v there, then the
     split-KV decode (split + combine kernels) attends over L_b + 1 rows; the
@@ -329,9 +329,10 @@ def bench_varlen(dev, rank, world, steps, warmup, dist):
     import numpy as np
     import torch
     from alpacca_open_sourced_by_jt_b200 import device
+    from alpacca_open_sourced_by_jt_b200.longctx import place_sequences
     H, KV, D = VL["H"], VL["KV"], VL["D"]
     Ls_all = np.random.default_rng(2).integers(VL["Lmin"], VL["Lmax"] + 1, size=VL["B"])
-    Ls = Ls_all[rank::world]
+    Ls = Ls_all[place_sequences(Ls_all, world)[rank]]
     B = len(Ls)
     n_ctx = VL["Lmax"] + 1
     g = torch.Generator(device=dev).manual_seed(2 + rank)
@@ -396,7 +397,8 @@ def bench_varlen(dev, rank, world, steps, warmup, dist):
             "scaling": "strong", "bytes_per_step": per_step, "split_rows": split,
             "seqs_per_gpu": B, "gpu_launches_per_step": 3,
             "achieved_per_gpu_max": round(local / (ms / nsteps * 1e-3) / 1e9, 1),
-            "config": "one batch of 64 seqs sharded by sequence over the GPUs, L_b ~ "
+            "config": "one batch of 64 seqs sharded by sequence over the GPUs (balanced "
+                      "by rows), L_b ~ "
                       f"U[1024,8192] (seed 2; mean {float(Ls_all.mean()):.0f}), 32 q / 8 KV "
                       "heads, D=128, fp16 KV; per step (one CUDA graph): fused RoPE+append "
                       "of each new token at L_b, split-KV decode over L_b+1 rows; KV bytes > "

@@ -14,7 +14,8 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle
-from alpacca_open_sourced_by_jt_b200.longctx import LongContextDecoder, shard_lengths, shard_rows
+from alpacca_open_sourced_by_jt_b200.longctx import (LongContextDecoder, place_sequences,
+                                                     shard_lengths, shard_rows)
 
 
 def test_shard_rows_cover_exactly():
@@ -29,6 +30,34 @@ def test_shard_rows_cover_exactly():
     assert shard_lengths([10, 3], 1, 4) == [3, 1]
     with pytest.raises(ValueError):
         shard_rows(5, 2, 2)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_place_sequences_balances_rows(world):
+    lens = np.random.default_rng(2).integers(1024, 8192 + 1, size=64)
+    placed = place_sequences(lens, world)
+    assert len(placed) == world
+    assert sorted(i for p in placed for i in p) == list(range(64))  # each sequence once
+    counts = [len(p) for p in placed]
+    assert max(counts) - min(counts) <= 1
+    assert all(p == sorted(p) for p in placed)
+    loads = [int(lens[p].sum()) for p in placed]
+    dealt = [int(lens[r::world].sum()) for r in range(world)]
+    assert max(loads) <= max(dealt)
+    # within one sequence's length of a perfect split
+    assert max(loads) - lens.sum() / world <= lens.max()
+    if world == 8:
+        assert max(loads) / (lens.sum() / world) < 1.02
+
+
+def test_place_sequences_edges():
+    assert place_sequences([], 4) == [[], [], [], []]
+    assert place_sequences([5], 3) == [[0], [], []]
+    assert place_sequences([1, 9, 9, 1], 2) == [[0, 1], [2, 3]]
+    with pytest.raises(ValueError):
+        place_sequences([3], 0)
+    with pytest.raises(ValueError):
+        place_sequences([-1], 2)
 
 
 def _free_port():
