@@ -105,6 +105,13 @@ SIGNATURES = [
     ("b2a_gemm_qkv_rope", c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_int, c_int,
                                   c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                   c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+    ("b2a_gemm_q8", c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_void_p, c_longlong,
+                            c_int, c_void_p, c_longlong, c_void_p, c_longlong, c_int, c_int,
+                            c_int, c_int, c_int, c_void_p]),
+    ("b2a_gemm_qkv_rope_q8", c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_void_p,
+                                     c_longlong, c_int, c_int, c_int, c_void_p, c_void_p,
+                                     c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                                     c_void_p, c_int, c_void_p]),
 ]
 
 _lib = None

@@ -336,7 +336,7 @@ def imrope_append(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, lanes: torc
     return q_out
 
 
-GEMM_STORE, GEMM_SWIGLU = 0, 1
+GEMM_STORE, GEMM_SWIGLU, GEMM_SWIGLU8 = 0, 1, 2
 
 
 def gemm(a: torch.Tensor, w: torch.Tensor, *, out=None, out_dtype=torch.float32, c_in=None,
@@ -366,6 +366,45 @@ def gemm(a: torch.Tensor, w: torch.Tensor, *, out=None, out_dtype=torch.float32,
     return out
 
 
+def _q8_parts(q8):
+    """(codes, scales) of a Q8_0 matrix: a Q8Matrix or a (codes, scales) pair,
+    codes int8 (N, K) and scales f16 (N, K/32), each with unit stride along K."""
+    codes, scales = (q8.codes, q8.scales) if hasattr(q8, "codes") else q8
+    _need(codes.dtype == torch.int8 and codes.dim() == 2 and codes.stride(1) == 1 and codes.is_cuda,
+          "codes int8 (N, K) on the device, unit stride along K")
+    N, K = codes.shape
+    _need(scales.dtype == torch.float16 and scales.shape == (N, K // 32) and scales.stride(1) == 1
+          and scales.is_cuda, "scales f16 (N, K/32) on the device")
+    return codes, scales
+
+
+def gemm_q8(a: torch.Tensor, q8, *, out=None, out_dtype=torch.float32, c_in=None,
+            epilogue: int = GEMM_STORE, stream=None) -> torch.Tensor:
+    """gemm() with Q8_0 weights decoded inside the kernel (b2a_gemm_q8): the
+    result equals gemm(a, d * code rounded to a's dtype).  q8 is a Q8Matrix
+    or (codes int8 (N, K), scales f16 (N, K/32)); a (M, K) f16 or bf16.
+    GEMM_SWIGLU8 takes the decode GEMV's gate/up layout (16-row groups of 8
+    gate rows then their 8 up rows) and writes silu(gate) * up, (M, N / 2)."""
+    codes, scales = _q8_parts(q8)
+    _need(a.dim() == 2 and a.shape[1] == codes.shape[1], "a (M, K), codes (N, K)")
+    _need(a.dtype in (torch.float16, torch.bfloat16) and a.stride(1) == 1,
+          "a f16 or bf16 with unit stride along K")
+    M, K = a.shape
+    N = codes.shape[0]
+    cols = N // 2 if epilogue in (GEMM_SWIGLU, GEMM_SWIGLU8) else N
+    if out is None:
+        out = torch.empty((M, cols), dtype=out_dtype, device=a.device)
+    _need(out.dim() == 2 and out.shape == (M, cols) and out.stride(1) == 1, "out (M, cols)")
+    if c_in is not None:
+        _need(c_in.dtype == torch.float32 and c_in.shape == (M, N) and c_in.stride(1) == 1,
+              "c_in f32 (M, N)")
+    _lib.check(_lib.load().b2a_gemm_q8(
+        _ptr(a), a.stride(0), _ptr(codes), codes.stride(0), _ptr(scales), scales.stride(0),
+        _code(a.dtype), _ptr(c_in), 0 if c_in is None else c_in.stride(0), _ptr(out),
+        out.stride(0), _code(out.dtype), M, N, K, int(epilogue), _stream(stream)))
+    return out
+
+
 def gemm_qkv_rope(a: torch.Tensor, w: torch.Tensor, positions: torch.Tensor,
                   cos_tab: torch.Tensor, sin_tab: torch.Tensor, *, H: int, KV: int, k_cache,
                   v_cache, q_out, stream=None) -> torch.Tensor:
@@ -376,10 +415,20 @@ def gemm_qkv_rope(a: torch.Tensor, w: torch.Tensor, positions: torch.Tensor,
     a (M, K) and w ((H + 2*KV)*D, K) 16-bit, unit stride along K; caches
     (n_ctx, KV, D) or (1, n_ctx, KV, D) of a's dtype; cos/sin f32 (rows,
     D/2): norm-style RoPE over the whole head.  The same result as gemm()
-    to f32 followed by rope_append(q_out=...)."""
-    _need(a.dim() == 2 and w.dim() == 2 and a.shape[1] == w.shape[1], "a (M,K), w (N,K)")
-    _need(a.dtype == w.dtype and a.dtype in (torch.float16, torch.bfloat16), "16-bit a and w")
-    _need(a.stride(1) == 1 and w.stride(1) == 1, "a and w need unit stride along K")
+    to f32 followed by rope_append(q_out=...).  w may also be Q8_0 weights
+    (a Q8Matrix or (codes, scales), as gemm_q8 takes them)."""
+    q8 = not isinstance(w, torch.Tensor)
+    if q8:  # Q8_0 weights (a Q8Matrix or (codes, scales)): b2a_gemm_qkv_rope_q8
+        codes, scales = _q8_parts(w)
+        w = codes
+        _need(a.dim() == 2 and a.shape[1] == codes.shape[1], "a (M,K), codes (N,K)")
+        _need(a.dtype in (torch.float16, torch.bfloat16) and a.stride(1) == 1,
+              "a f16 or bf16 with unit stride along K")
+    else:
+        _need(a.dim() == 2 and w.dim() == 2 and a.shape[1] == w.shape[1], "a (M,K), w (N,K)")
+        _need(a.dtype == w.dtype and a.dtype in (torch.float16, torch.bfloat16),
+              "16-bit a and w")
+        _need(a.stride(1) == 1 and w.stride(1) == 1, "a and w need unit stride along K")
     M, K = a.shape
     if k_cache.dim() == 4:
         _need(k_cache.shape[0] == 1 and v_cache.shape[0] == 1, "one sequence's cache")
@@ -396,6 +445,13 @@ def gemm_qkv_rope(a: torch.Tensor, w: torch.Tensor, positions: torch.Tensor,
     _need(positions.dtype == torch.int32 and positions.numel() == M, "positions int32 (M,)")
     _need(cos_tab.shape == sin_tab.shape and cos_tab.shape[1] * 2 == D,
           "cos/sin tables (rows, D/2)")
+    if q8:
+        _lib.check(_lib.load().b2a_gemm_qkv_rope_q8(
+            _ptr(a), a.stride(0), _ptr(codes), codes.stride(0), _ptr(scales), scales.stride(0),
+            _code(a.dtype), M, K, _ptr(positions), _ptr(cos_tab), _ptr(sin_tab),
+            cos_tab.shape[0], H, KV, D, _ptr(q_out), _ptr(k_cache), _ptr(v_cache), n_ctx,
+            _stream(stream)))
+        return q_out
     _lib.check(_lib.load().b2a_gemm_qkv_rope(
         _ptr(a), a.stride(0), _ptr(w), w.stride(0), _code(a.dtype), M, K, _ptr(positions),
         _ptr(cos_tab), _ptr(sin_tab), cos_tab.shape[0], H, KV, D, _ptr(q_out), _ptr(k_cache),

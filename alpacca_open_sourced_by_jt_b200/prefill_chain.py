@@ -22,8 +22,16 @@ straight into a DecodeChain's caches, so decoding continues from it:
     x   += act . Wdown^T   b2a_gemm, residual in the epilogue
   logits = Woutput . RMSNorm(x[T-1])   b2a_q8_gemv (the decode path's Q8_0 GEMV)
 
-The GEMMs run on 16-bit dequantized weights (d * code, one copy per matrix
-made at set-up) with fp32 accumulation.  The 16-bit operands are the one
+weights="f16" (the default): one 16-bit dequantized copy per matrix made at
+set-up (2 bytes per weight) and the plain b2a_gemm.
+weights="q8": the GEMMs read the decode chain's own Q8_0 matrices
+(b2a_gemm_q8 / b2a_gemm_qkv_rope_q8: int8 codes into shared memory, d * code
+written as 16-bit operand tiles inside the kernel), as the reference's
+codes-decoding GEMM does, and the gate/up product takes the GEMV's 8-row
+interleave (GEMM_SWIGLU8): no weight copy at all, for when the copy does not
+fit; on one B200 its config-5 chunk takes 8.0 ms against 4.6 ms.
+Both give the same products bit for bit (the in-place residuals up to their
+summation order); the 16-bit operands with fp32 accumulation are the one
 precision step away from the reference's f32 SIMT GEMM.
 """
 from __future__ import annotations
@@ -45,7 +53,7 @@ class ChunkPrefill:
     """Prefill chunks of up to max_chunk tokens into `chain`'s caches (which
     must be f16 or bf16: the attention runs on the tcgen05 prefill kernel)."""
 
-    def __init__(self, chain: DecodeChain, max_chunk: int = 256):
+    def __init__(self, chain: DecodeChain, max_chunk: int = 256, weights: str = "f16"):
         _lib.load()
         m = chain.m
         self.chain, self.m = chain, m
@@ -55,12 +63,21 @@ class ChunkPrefill:
         self.dt, self.code = dt, device._code(dt)
         dev = m.device
         self.max_chunk = int(max_chunk)
-        if m.F % 128:
-            raise _lib.B2AShapeError(_lib.ERR_SHAPE, "chunk prefill needs n_ff % 128 == 0")
-        self.w = [dict(qkv=_dequant(ly["wqkv"], dt), wo=_dequant(ly["wo"], dt),
-                       gu=self._gate_up(_dequant(ly["wgu"], dt), m.F),
-                       down=_dequant(ly["w_down"], dt))
-                  for ly in m.layers]
+        if weights == "q8":
+            if m.F % 8:  # the gate/up matrix's rows: 16-row groups of 8 gate + 8 up
+                raise _lib.B2AShapeError(_lib.ERR_SHAPE, "Q8_0 chunk GEMMs need n_ff % 8 == 0")
+            self.w = [dict(qkv=ly["wqkv"], wo=ly["wo"], gu=ly["wgu"], down=ly["w_down"])
+                      for ly in m.layers]
+        elif weights == "f16":
+            if m.F % 128:
+                raise _lib.B2AShapeError(_lib.ERR_SHAPE, "16-bit chunk GEMMs need n_ff % 128 == 0")
+            self.w = [dict(qkv=_dequant(ly["wqkv"], dt), wo=_dequant(ly["wo"], dt),
+                           gu=self._gate_up(_dequant(ly["wgu"], dt), m.F),
+                           down=_dequant(ly["w_down"], dt))
+                      for ly in m.layers]
+        else:
+            raise _lib.B2AError(_lib.ERR_ARG, f"weights {weights!r} (q8 or f16)")
+        self.weights = weights
         T, E, H, KV, D, F = self.max_chunk, m.E, m.H, m.KV, m.D, m.F
         self.x = torch.zeros((T, E), dtype=torch.float32, device=dev)
         self.h = torch.zeros((T, E), dtype=dt, device=dev)
@@ -118,10 +135,16 @@ class ChunkPrefill:
                                  q_out=self.qrot[:T])
             att = device.prefill(self.qrot[:T], ch.k_cache[li][0, :t_kv],
                                  ch.v_cache[li][0, :t_kv], pos, out=self.att[:T])
-            device.gemm(att.view(T, qd), w["wo"], out=x, c_in=x)
-            h = self._norm(x, ly["ffn_norm"], T)
-            device.gemm(h, w["gu"], out=self.act[:T], epilogue=device.GEMM_SWIGLU)
-            device.gemm(self.act[:T], w["down"], out=x, c_in=x)
+            if self.weights == "q8":
+                device.gemm_q8(att.view(T, qd), w["wo"], out=x, c_in=x)
+                h = self._norm(x, ly["ffn_norm"], T)
+                device.gemm_q8(h, w["gu"], out=self.act[:T], epilogue=device.GEMM_SWIGLU8)
+                device.gemm_q8(self.act[:T], w["down"], out=x, c_in=x)
+            else:
+                device.gemm(att.view(T, qd), w["wo"], out=x, c_in=x)
+                h = self._norm(x, ly["ffn_norm"], T)
+                device.gemm(h, w["gu"], out=self.act[:T], epilogue=device.GEMM_SWIGLU)
+                device.gemm(self.act[:T], w["down"], out=x, c_in=x)
         if not want_logits:
             return None
         m.output.gemv(x[T - 1], self.logits, mode=1, aux=m.out_norm, eps=m.eps, flags=PDL)

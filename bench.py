@@ -615,17 +615,23 @@ def bench_gemm(dev, steps, warmup):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / n * 1e3  # us
 
+    from alpacca_open_sourced_by_jt_b200.decode_chain import Q8Matrix
     hbm, bf16, bf16_sus, src = peaks()
-    out, tot_fl, tot_us = {}, 0.0, 0.0
+    out, tot_fl, tot_us, tot_us8 = {}, 0.0, 0.0, 0.0
     for name, N, K, epi in shapes:
         a = torch.randn((T, K), device=dev, generator=g).to(torch.float16)
-        w = (0.02 * torch.randn((N, K), device=dev, generator=g)).to(torch.float16)
+        w32 = 0.02 * torch.randn((N, K), device=dev, generator=g)
+        w = w32.to(torch.float16)
+        q8 = Q8Matrix.quantize(w32)  # the same matrix as Q8_0 codes + scales
+        del w32
         if epi == "swiglu":
             o = torch.empty((T, N // 2), device=dev, dtype=torch.float16)
             fn = lambda: device.gemm(a, w, out=o, epilogue=device.GEMM_SWIGLU)
+            fn8 = lambda: device.gemm_q8(a, q8, out=o, epilogue=device.GEMM_SWIGLU8)
         elif epi == "residual":
             o = torch.zeros((T, N), device=dev)
             fn = lambda: device.gemm(a, w, out=o, c_in=o)
+            fn8 = lambda: device.gemm_q8(a, q8, out=o, c_in=o)
         elif epi == "rope":
             H, KV, D = C5["n_head"], C5["n_kv"], C5["head_dim"]
             cos, sin = device.rope_tables(T, D, 10000.0, device=dev)
@@ -635,24 +641,34 @@ def bench_gemm(dev, steps, warmup):
             o = torch.empty((T, H, D), device=dev, dtype=torch.float16)
             fn = lambda: device.gemm_qkv_rope(a, w, pos, cos, sin, H=H, KV=KV, k_cache=kc,
                                               v_cache=vc, q_out=o)
+            fn8 = lambda: device.gemm_qkv_rope(a, q8, pos, cos, sin, H=H, KV=KV, k_cache=kc,
+                                               v_cache=vc, q_out=o)
         else:
             o = torch.empty((T, N), device=dev)
             fn = lambda: device.gemm(a, w, out=o)
+            fn8 = lambda: device.gemm_q8(a, q8, out=o)
         us = timed(fn)
+        us8 = timed(fn8)
         ref = timed(lambda: torch.mm(a, w.t(), out_dtype=torch.float32))
         fl = 2.0 * T * N * K
         tot_fl += fl
         tot_us += us
+        tot_us8 += us8
         out[name] = {"M": T, "N": N, "K": K, "epilogue": epi, "us": round(us, 1),
                      "tflops": round(fl / us / 1e6, 1), "frac": round(fl / us / 1e6 / bf16, 4),
+                     "q8_us": round(us8, 1), "q8_tflops": round(fl / us8 / 1e6, 1),
                      "cublas_tflops_plain": round(fl / ref / 1e6, 1)}
-        del a, w, o
+        del a, w, o, q8
     tf = tot_fl / tot_us / 1e6
+    tf8 = tot_fl / tot_us8 / 1e6
     return {"metric": "prefill-chunk GEMM TFLOPS (config-5 shapes, 2048 tokens)",
             "value": round(tf, 1), "unit": "TFLOP/s", "launches": 4 * n,
             "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": bf16,
                          "unit": "TFLOP/s", "frac": round(tf / bf16, 4),
                          "peak_source": f"{src} (MEASURED_PEAKS.json bf16_tflops, burst)"},
+            "q8_weights": {"value": round(tf8, 1), "unit": "TFLOP/s",
+                           "frac": round(tf8 / bf16, 4),
+                           "note": "b2a_gemm_q8: Q8_0 codes decoded to f16 inside the kernel"},
             "shapes": out}
 
 
@@ -667,19 +683,28 @@ def bench_prefill_chunk(dev, steps, warmup):
     T, n_ctx = 2048, 4096
     m = LlamaQ8.random(**C5, seed=5, dev=dev)
     chain = DecodeChain(m, n_ctx, torch.float16)
-    pre = ChunkPrefill(chain, max_chunk=T)
     toks = [(7 * i + 3) % C5["n_vocab"] for i in range(T)]
-    for _ in range(max(2, min(warmup, 3))):
-        pre(toks, 0, want_logits=False)
     n = max(3, min(steps, 10))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(n):
-        pre(toks, 0, want_logits=False)
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / n
+
+    def time_chunk(pre):
+        for _ in range(max(2, min(warmup, 3))):
+            pre(toks, 0, want_logits=False)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(n):
+            pre(toks, 0, want_logits=False)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    # the Q8_0 in-kernel path (no weight copy), for comparison, then the default
+    # (a 16-bit weight copy)
+    pre8 = ChunkPrefill(chain, max_chunk=T, weights="q8")
+    ms8 = time_chunk(pre8)
+    del pre8
+    pre = ChunkPrefill(chain, max_chunk=T)
+    ms = time_chunk(pre)
     E, H, KV, D, F, L = (C5["n_embd"], C5["n_head"], C5["n_kv"], C5["head_dim"], C5["n_ff"],
                          C5["n_layer"])
     w_layer = E * (H + 2 * KV) * D + H * D * E + 2 * F * E + F * E
@@ -689,12 +714,14 @@ def bench_prefill_chunk(dev, steps, warmup):
     del pre, chain, m
     return {"metric": "prefill chunk tokens/s (config-5 model, 2048-token chunk)",
             "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_chunk": round(ms, 3),
-            "tflops": round(tf, 1), "steps": n,
+            "tflops": round(tf, 1), "steps": n, "weights": "f16 copy",
+            "ms_per_chunk_q8_in_kernel": round(ms8, 3),
             "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": bf16,
                          "unit": "TFLOP/s", "frac": round(tf / bf16, 4),
                          "peak_source": f"{src} (MEASURED_PEAKS.json bf16_tflops, burst)"},
             "config": "16 layers, hidden 2048, 32/8 heads x 64, FFN 8192, vocab 128256; "
-                      "weights dequantized to f16; every kernel this library's: tcgen05 GEMMs "
+                      "weights dequantized to f16 (ms_per_chunk_q8_in_kernel: the GEMMs decoding "
+                      "the Q8_0 codes instead); every kernel this library's: tcgen05 GEMMs "
                       "(RoPE + K/V append, residual add and SwiGLU in their epilogues), RMSNorm, "
                       "tcgen05 causal prefill; eager launches (7 per layer)"}
 

@@ -437,6 +437,37 @@ int b2a_gemm_qkv_rope(const void* a, long long lda, const void* w, long long ldw
                       int tab_rows, int H, int KV, int D, void* q_out, void* k_cache,
                       void* v_cache, int n_ctx, void* stream);
 
+/* The same GEMMs straight from Q8_0 weights, the way the reference's chunk
+ * GEMM reads them (the codes-decoding GEMM, cuda.py:287-422, with
+ * Q8_0 records of quants.py: a f16 scale d per 32 codes): no 16-bit weight
+ * copy exists.  The kernel loads the int8 codes with TMA and converter warps
+ * write d * code, rounded once to dtype, into the tensor cores' operand
+ * tiles in shared memory, so the product equals b2a_gemm's on the
+ * dequantized matrix (bit for bit, except the summation order of an
+ * in-place residual split over CTAs).
+ *   codes int8 [N][ldq] (row n, code k at n*ldq + k), 16-byte aligned,
+ *         ldq >= K and a multiple of 16
+ *   scales f16 [N][lds]: the scale of codes 32b..32b+31 of row n at
+ *         n*lds + b, lds >= K/32
+ * K a multiple of 32.  Epilogues as b2a_gemm's, plus
+ *   B2A_GEMM_SWIGLU8 out[m][8g + j] = silu(s[16g + j]) * s[16g + 8 + j]
+ *                    (j < 8): rows in 16-row groups of 8 gate rows then the
+ *                    matching 8 up rows, the layout b2a_q8_gemv's
+ *                    B2A_GEMV_SWIGLU_OUT reads; N % 16 == 0, no c_in. */
+#define B2A_GEMM_SWIGLU8 2
+int b2a_gemm_q8(const void* a, long long lda, const void* codes, long long ldq,
+                const void* scales, long long lds, int dtype, const float* c_in, long long ldc,
+                void* out, long long ldo, int out_dtype, int M, int N, int K, int epilogue,
+                void* stream);
+
+/* b2a_gemm_qkv_rope from Q8_0 weights (codes and scales as b2a_gemm_q8,
+ * N = (H + 2*KV)*D rows [q; k; v]). */
+int b2a_gemm_qkv_rope_q8(const void* a, long long lda, const void* codes, long long ldq,
+                         const void* scales, long long lds, int dtype, int M, int K,
+                         const int* pos_dev, const float* cos_tab, const float* sin_tab,
+                         int tab_rows, int H, int KV, int D, void* q_out, void* k_cache,
+                         void* v_cache, int n_ctx, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -5,10 +5,12 @@ tests/golden/llama_q8.npz holds, for the small Q8_0 llama model, the logits
 of the reference's Model.forward_batch on the first five tokens as one chunk
 (alpaccaroo/model.py:1274-1372), its layer-0 K rows, and the logits of the
 decode token that follows.  The chunk runs its GEMMs on 16-bit dequantized
-weights and activations (f32 accumulation) and its attention on the 16-bit
+weights (decoded inside the kernel from the Q8_0 codes, or a 16-bit copy made
+at set-up) and activations (f32 accumulation) and its attention on the 16-bit
 cache, so the bar is 2e-2 normwise on the logits and 2e-2 absolute on the
 stored K rows; the same chunk split in two (the second attending over the
-first's cached rows) must agree with the single chunk.
+first's cached rows) must agree with the single chunk, and the two weight
+paths must agree with each other to fp32 rounding.
 """
 import numpy as np
 import pytest
@@ -20,9 +22,10 @@ from tests.golden import cases
 pytestmark = pytest.mark.gpu
 
 
+@pytest.mark.parametrize("weights", ["q8", "f16"])
 @pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("split", [None, 3])
-def test_chunk_prefill_matches_reference(cuda_dev, golden, dt, split):
+def test_chunk_prefill_matches_reference(cuda_dev, golden, dt, split, weights):
     from alpacca_open_sourced_by_jt_b200.decode_chain import DecodeChain, LlamaQ8
     from alpacca_open_sourced_by_jt_b200.prefill_chain import ChunkPrefill
     g = golden("llama_q8.npz")
@@ -30,7 +33,7 @@ def test_chunk_prefill_matches_reference(cuda_dev, golden, dt, split):
     assert c["sha256"] == str(g["weights_sha256"])
     n = int(g["n_chunk"])
     chain = DecodeChain(LlamaQ8.from_spec(c, cuda_dev), c["n_ctx"], dt)
-    pre = ChunkPrefill(chain, max_chunk=8)
+    pre = ChunkPrefill(chain, max_chunk=8, weights=weights)
     if split is None:
         logits = pre(c["tokens"][:n], 0)
     else:
@@ -61,3 +64,20 @@ def test_chunk_prefill_rejects_bad_requests(cuda_dev):
     with pytest.raises(_lib.B2AError):
         pre([c["n_vocab"]], 0)
     assert np.isfinite(pre([1, 2], 0)).all()
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_chunk_q8_weights_equal_16bit_copy(cuda_dev, dt):
+    """The in-kernel Q8_0 decode gives the products of the 16-bit copy: the
+    same logits and K/V rows up to the residual sums' order."""
+    from alpacca_open_sourced_by_jt_b200.decode_chain import DecodeChain, LlamaQ8
+    from alpacca_open_sourced_by_jt_b200.prefill_chain import ChunkPrefill
+    c = cases.llama_q8_case()
+    model = LlamaQ8.from_spec(c, cuda_dev)
+    res = []
+    for weights in ("q8", "f16"):
+        chain = DecodeChain(model, c["n_ctx"], dt)
+        logits = ChunkPrefill(chain, max_chunk=8, weights=weights)(c["tokens"][:6], 0)
+        res.append((logits, chain.k_cache[1][0, :6].float().cpu().numpy()))
+    assert rel_err(res[0][0], res[1][0]) < 1e-5
+    assert max_abs_err(res[0][1], res[1][1]) < 1e-2  # one 16-bit rounding apart at most
