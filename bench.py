@@ -441,6 +441,9 @@ def bench_kvstate(dev, steps, warmup):
     ms_w = timed(lambda: convert(k16, f32), reps)
     ms_n = timed(lambda: convert(f32, k16b), reps)
     assert torch.equal(k16b, k16)  # narrow(widen(x)) == x for 16-bit x
+    # the same widening by torch (its elementwise copy kernel), for the
+    # write-heavy traffic's own ceiling on this part
+    ms_tw = timed(lambda: f32.copy_(k16), reps)
     st.snapshot()
     t0 = time.perf_counter()
     for _ in range(3):
@@ -453,6 +456,7 @@ def bench_kvstate(dev, steps, warmup):
             "value": round(gbs_w, 1), "unit": "GB/s", "ms_per_launch": round(ms_w, 4),
             "narrow_gbs": round(bytes_conv / (ms_n * 1e-3) / 1e9, 1),
             "narrow_ms_per_launch": round(ms_n, 4),
+            "torch_widen_gbs": round(bytes_conv / (ms_tw * 1e-3) / 1e9, 1),
             "snapshot_layer_ms": round(ms_s, 2),
             "snapshot_layer_gbs": round(snap.memory_bytes() / (ms_s * 1e-3) / 1e9, 2),
             "roofline": {"bound": "hbm", "achieved": round(gbs_w, 1), "peak": hbm,
