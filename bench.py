@@ -907,6 +907,22 @@ def run_ours(args):
         # every rank runs its own end-to-end loop at the same time; the
         # slowest rank's step time counts for all
         e2e = bench_e2e(dev, st, args.steps, args.warmup, dist)
+    # config 2 head-sharded over the ranks (rank r: KV heads r*KV/N .. and their
+    # q heads, the whole sequence; no collective), max over ranks of each
+    # launch's CUDA-event time; every rank runs it, so it comes before the
+    # rank-0 legs
+    pf_sh = None
+    if world > 1 and PF["KV"] % world == 0 and args.only in (None, "prefill") \
+            and not args.no_prefill:
+        sh = bench_prefill(dev, args.steps, args.warmup,
+                           shape=(PF["S"], PF["H"] // world, PF["KV"] // world, PF["D"]))
+        t = torch.tensor([sh["ms"]], device=dev)
+        dist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        ms_sh = float(t.item())
+        pf_sh = {"ms": ms_sh, "tflops": prefill_flops(PF["S"], PF["H"], PF["D"]) / (ms_sh * 1e-3)
+                 / 1e12, "kv_heads_per_gpu": PF["KV"] // world, "q_heads_per_gpu": PF["H"] // world}
+        del sh
+        dist.barrier()
     if rank == 0:
         pf = pf256 = None
         if args.only in (None, "prefill") and not args.no_prefill:
@@ -986,6 +1002,15 @@ def run_ours(args):
                                  "frac": round(pf256["tflops"] / bf16, 4)}}
             if pcpu:
                 result["prefill"]["cpu_baseline"] = pcpu
+            if pf_sh:
+                result["prefill"]["head_sharded"] = {
+                    "value": round(pf_sh["tflops"], 1), "unit": "TFLOP/s", "n_gpus": world,
+                    "scaling": "strong", "ms_per_launch": round(pf_sh["ms"], 4),
+                    "efficiency_vs_one_gpu_same_run": round(
+                        pf_sh["tflops"] / (world * pf["tflops"]), 4),
+                    "config": f"config 2 split by KV head: {pf_sh['kv_heads_per_gpu']} KV / "
+                              f"{pf_sh['q_heads_per_gpu']} q heads per GPU, whole sequence, no "
+                              "collective; time = max over ranks; FLOPs of the whole job"}
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
