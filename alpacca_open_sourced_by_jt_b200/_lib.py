@@ -108,6 +108,8 @@ SIGNATURES = [
     ("b2a_gemm_q8", c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_void_p, c_longlong,
                             c_int, c_void_p, c_longlong, c_void_p, c_longlong, c_int, c_int,
                             c_int, c_int, c_int, c_void_p]),
+    ("b2a_q8_dequant", c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_void_p, c_longlong,
+                               c_int, c_int, c_int, c_void_p]),
     ("b2a_gemm_qkv_rope_q8", c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_void_p,
                                      c_longlong, c_int, c_int, c_int, c_void_p, c_void_p,
                                      c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p,

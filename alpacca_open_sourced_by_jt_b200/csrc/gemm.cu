@@ -212,6 +212,55 @@ struct QkvRope {
   int tab_rows, n_ctx, H, KV, D;
 };
 
+// Q8_0 -> 16-bit rows (b2a_q8_dequant): out[r][k] = d[r][k/32] * code[r][k]
+// rounded once to T, the operand values the W8 converters write.  One item =
+// 16 codes (a 16-byte load, two 16-byte stores); each thread takes two items
+// per round, both loads issued before either conversion, grid-strided with
+// 32-bit index arithmetic (the host keeps rows * cols / 16 below 2^31).
+// HBM-bound at 3 + 1/16 bytes per weight.
+template <typename T>
+__global__ void __launch_bounds__(256) q8_dequant_kernel(const int8_t* __restrict__ codes,
+                                                         long long ldq,
+                                                         const __half* __restrict__ scales,
+                                                         long long lds, T* __restrict__ out,
+                                                         long long ldo, int rows, int cols) {
+  const unsigned per_row = static_cast<unsigned>(cols) / 16u;
+  const unsigned total = static_cast<unsigned>(rows) * per_row;
+  const unsigned stride = gridDim.x * blockDim.x;
+  auto at = [&](unsigned i, unsigned& r, unsigned& c) {
+    r = i / per_row;
+    c = (i - r * per_row) * 16u;
+  };
+  unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + stride < total; i += 2 * stride) {
+    unsigned r0, c0, r1, c1;
+    at(i, r0, c0);
+    at(i + stride, r1, c1);
+    const uint4 q0 = __ldcs(reinterpret_cast<const uint4*>(codes + r0 * ldq + c0));
+    const uint4 q1 = __ldcs(reinterpret_cast<const uint4*>(codes + r1 * ldq + c1));
+    const __half d0 = scales[r0 * lds + c0 / 32], d1 = scales[r1 * lds + c1 / 32];
+    uint4 o0, o1;
+    Dequant<T>::run(q0, Dequant<T>::scale(d0), o0, o1);
+    uint4* dst = reinterpret_cast<uint4*>(out + r0 * ldo + c0);
+    dst[0] = o0;
+    dst[1] = o1;
+    Dequant<T>::run(q1, Dequant<T>::scale(d1), o0, o1);
+    dst = reinterpret_cast<uint4*>(out + r1 * ldo + c1);
+    dst[0] = o0;
+    dst[1] = o1;
+  }
+  if (i < total) {
+    unsigned r, c;
+    at(i, r, c);
+    const uint4 q = __ldcs(reinterpret_cast<const uint4*>(codes + r * ldq + c));
+    uint4 o0, o1;
+    Dequant<T>::run(q, Dequant<T>::scale(scales[r * lds + c / 32]), o0, o1);
+    uint4* dst = reinterpret_cast<uint4*>(out + r * ldo + c);
+    dst[0] = o0;
+    dst[1] = o1;
+  }
+}
+
 // The CTA's work as segments (tile, first K-block, end K-block).  Tiles
 // (SK false): whole tiles t = c, c + G, ...  Stream-K (SK true): the
 // tiles x K-blocks iterations split evenly over the grid, so every CTA does
@@ -902,9 +951,9 @@ int b2a_gemm(const void* a, long long lda, const void* w, long long ldw, int dty
   if (!b2a_host::aligned16(a) || !b2a_host::aligned16(w) || !b2a_host::aligned16(out) ||
       (c_in && !b2a_host::aligned16(c_in)))
     return fail(B2A_ERR_ALIGN, "gemm: a, w, c_in and out must be 16-byte aligned");
-  if (epilogue != B2A_GEMM_STORE && epilogue != B2A_GEMM_SWIGLU)
+  if (epilogue != B2A_GEMM_STORE && epilogue != B2A_GEMM_SWIGLU && epilogue != B2A_GEMM_SWIGLU8)
     return fail(B2A_ERR_ARG, "gemm: epilogue %d", epilogue);
-  const int out_cols = epilogue == B2A_GEMM_SWIGLU ? N / 2 : N;
+  const int out_cols = epilogue != B2A_GEMM_STORE ? N / 2 : N;
   if (ldo < out_cols || (c_in && ldc < N))
     return fail(B2A_ERR_SHAPE, "gemm: ldo/ldc smaller than the row");
   const int eb = b2a_host::elem_size(out_dtype);
@@ -913,15 +962,23 @@ int b2a_gemm(const void* a, long long lda, const void* w, long long ldw, int dty
     return fail(B2A_ERR_ALIGN, "gemm: output and c_in rows must start on 16-byte boundaries");
   if (epilogue == B2A_GEMM_SWIGLU && (N % 256 || c_in))
     return fail(B2A_ERR_SHAPE, "gemm: SWIGLU needs N a multiple of 256 and no c_in");
+  if (epilogue == B2A_GEMM_SWIGLU8 && (N % 16 || c_in))
+    return fail(B2A_ERR_SHAPE, "gemm: SWIGLU8 needs N a multiple of 16 and no c_in");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == B2A_BF16)
-    return epilogue == B2A_GEMM_SWIGLU
-               ? gemm_out<__nv_bfloat16, 1>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st)
-               : gemm_out<__nv_bfloat16, 0>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
-  if (dtype == B2A_F16)
-    return epilogue == B2A_GEMM_SWIGLU
-               ? gemm_out<__half, 1>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st)
-               : gemm_out<__half, 0>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
+  if (dtype == B2A_BF16) {
+    if (epilogue == B2A_GEMM_SWIGLU)
+      return gemm_out<__nv_bfloat16, 1>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
+    if (epilogue == B2A_GEMM_SWIGLU8)
+      return gemm_out<__nv_bfloat16, 4>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
+    return gemm_out<__nv_bfloat16, 0>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
+  }
+  if (dtype == B2A_F16) {
+    if (epilogue == B2A_GEMM_SWIGLU)
+      return gemm_out<__half, 1>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
+    if (epilogue == B2A_GEMM_SWIGLU8)
+      return gemm_out<__half, 4>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
+    return gemm_out<__half, 0>(out_dtype, a, lda, w, ldw, c_in, ldc, out, ldo, M, N, K, st);
+  }
   return fail(B2A_ERR_DTYPE, "gemm: operand dtype %d (f16 or bf16)", dtype);
 }
 
@@ -1041,6 +1098,37 @@ int b2a_gemm_qkv_rope_q8(const void* a, long long lda, const void* codes, long l
     return launch_gemm_q8_auto<__half, __half, 2>(a, lda, codes, ldq, scales, lds, nullptr, 0,
                                                   nullptr, 0, M, N, K, st, rp);
   return fail(B2A_ERR_DTYPE, "gemm_qkv_rope_q8: dtype %d (f16 or bf16)", dtype);
+}
+
+
+int b2a_q8_dequant(const void* codes, long long ldq, const void* scales, long long lds,
+                   void* out, long long ldo, int dtype, int rows, int cols, void* stream) {
+  using b2a_host::fail;
+  if (!out) return fail(B2A_ERR_ARG, "q8_dequant: null output");
+  if (rows <= 0 || cols <= 0) return fail(B2A_ERR_SHAPE, "q8_dequant: rows=%d cols=%d", rows, cols);
+  int rc = check_q8(codes, ldq, scales, lds, rows, cols, "q8_dequant");
+  if (rc) return rc;
+  if (ldo < cols || ldo % 8 || !b2a_host::aligned16(out))
+    return fail(B2A_ERR_ALIGN, "q8_dequant: out 16-byte aligned, ldo >= cols and a multiple of 8");
+  const long long work = static_cast<long long>(rows) * (cols / 16);
+  if (work >= (1LL << 31)) return fail(B2A_ERR_SHAPE, "q8_dequant: %d x %d is too large", rows, cols);
+  long long blocks = (work + 511) / 512;  // two items per thread
+  const long long cap = static_cast<long long>(b2a_host::sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int8_t* q = static_cast<const int8_t*>(codes);
+  const __half* sc = static_cast<const __half*>(scales);
+  if (dtype == B2A_F16)
+    b2a::gemm::q8_dequant_kernel<__half><<<static_cast<int>(blocks), 256, 0, st>>>(
+        q, ldq, sc, lds, static_cast<__half*>(out), ldo, rows, cols);
+  else if (dtype == B2A_BF16)
+    b2a::gemm::q8_dequant_kernel<__nv_bfloat16><<<static_cast<int>(blocks), 256, 0, st>>>(
+        q, ldq, sc, lds, static_cast<__nv_bfloat16*>(out), ldo, rows, cols);
+  else
+    return fail(B2A_ERR_DTYPE, "q8_dequant: dtype %d (f16 or bf16)", dtype);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return b2a_host::cuda_fail(e, "q8_dequant launch");
+  return B2A_OK;
 }
 
 }  // extern "C"

@@ -346,13 +346,14 @@ def gemm(a: torch.Tensor, w: torch.Tensor, *, out=None, out_dtype=torch.float32,
     a (M, K) and w (N, K) 16-bit with unit stride along K; c_in f32 (M, N)
     or None (may be out itself, for an in-place residual add).  With
     GEMM_SWIGLU, w's rows come in 256-row groups of 128 gate rows and the
-    matching 128 up rows and out is silu(gate) * up, (M, N / 2)."""
+    matching 128 up rows and out is silu(gate) * up, (M, N / 2); GEMM_SWIGLU8
+    takes 16-row groups of 8 gate then 8 up rows (the decode GEMV's layout)."""
     _need(a.dim() == 2 and w.dim() == 2 and a.shape[1] == w.shape[1], "a (M,K), w (N,K)")
     _need(a.dtype == w.dtype and a.dtype in (torch.float16, torch.bfloat16), "16-bit a and w")
     _need(a.stride(1) == 1 and w.stride(1) == 1, "a and w need unit stride along K")
     M, K = a.shape
     N = w.shape[0]
-    cols = N // 2 if epilogue == GEMM_SWIGLU else N
+    cols = N // 2 if epilogue in (GEMM_SWIGLU, GEMM_SWIGLU8) else N
     if out is None:
         out = torch.empty((M, cols), dtype=out_dtype, device=a.device)
     _need(out.dim() == 2 and out.shape == (M, cols) and out.stride(1) == 1, "out (M, cols)")
@@ -376,6 +377,23 @@ def _q8_parts(q8):
     _need(scales.dtype == torch.float16 and scales.shape == (N, K // 32) and scales.stride(1) == 1
           and scales.is_cuda, "scales f16 (N, K/32) on the device")
     return codes, scales
+
+
+def q8_dequant(q8, dtype=torch.float16, *, out=None, stream=None) -> torch.Tensor:
+    """Q8_0 matrix (a Q8Matrix or (codes, scales)) to 16-bit rows on the device
+    (b2a_q8_dequant): d * code rounded once to dtype, the values gemm_q8
+    feeds the tensor cores.  out, if given, is a (rows, cols) view with unit
+    stride along the columns."""
+    codes, scales = _q8_parts(q8)
+    N, K = codes.shape
+    if out is None:
+        out = torch.empty((N, K), dtype=dtype, device=codes.device)
+    _need(out.dtype in (torch.float16, torch.bfloat16) and out.shape == (N, K) and
+          out.stride(1) == 1, "out (rows, cols) f16 or bf16")
+    _lib.check(_lib.load().b2a_q8_dequant(
+        _ptr(codes), codes.stride(0), _ptr(scales), scales.stride(0), _ptr(out), out.stride(0),
+        _code(out.dtype), N, K, _stream(stream)))
+    return out
 
 
 def gemm_q8(a: torch.Tensor, q8, *, out=None, out_dtype=torch.float32, c_in=None,

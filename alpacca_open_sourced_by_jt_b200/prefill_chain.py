@@ -30,8 +30,12 @@ written as 16-bit operand tiles inside the kernel), as the reference's
 codes-decoding GEMM does, and the gate/up product takes the GEMV's 8-row
 interleave (GEMM_SWIGLU8): no weight copy at all, for when the copy does not
 fit; on one B200 its config-5 chunk takes 8.0 ms against 4.6 ms.
-Both give the same products bit for bit (the in-place residuals up to their
-summation order); the 16-bit operands with fp32 accumulation are the one
+weights="q8_dequant": the decode chain's Q8_0 matrices again, each turned
+into 16-bit rows (b2a_q8_dequant, HBM-bound) in one reusable buffer just
+before its b2a_gemm: the buffer holds the largest matrix (the gate/up rows,
+67 MB at config 5) instead of a copy of all of them.
+All three give the same products bit for bit (the in-place residuals up to
+their summation order); the 16-bit operands with fp32 accumulation are the one
 precision step away from the reference's f32 SIMT GEMM.
 """
 from __future__ import annotations
@@ -63,11 +67,15 @@ class ChunkPrefill:
         self.dt, self.code = dt, device._code(dt)
         dev = m.device
         self.max_chunk = int(max_chunk)
-        if weights == "q8":
+        self.scratch = None
+        if weights in ("q8", "q8_dequant"):
             if m.F % 8:  # the gate/up matrix's rows: 16-row groups of 8 gate + 8 up
                 raise _lib.B2AShapeError(_lib.ERR_SHAPE, "Q8_0 chunk GEMMs need n_ff % 8 == 0")
             self.w = [dict(qkv=ly["wqkv"], wo=ly["wo"], gu=ly["wgu"], down=ly["w_down"])
                       for ly in m.layers]
+            if weights == "q8_dequant":
+                biggest = max(q.rows * q.cols for q in self.w[0].values())
+                self.scratch = torch.empty(biggest, dtype=dt, device=dev)
         elif weights == "f16":
             if m.F % 128:
                 raise _lib.B2AShapeError(_lib.ERR_SHAPE, "16-bit chunk GEMMs need n_ff % 128 == 0")
@@ -76,7 +84,7 @@ class ChunkPrefill:
                            down=_dequant(ly["w_down"], dt))
                       for ly in m.layers]
         else:
-            raise _lib.B2AError(_lib.ERR_ARG, f"weights {weights!r} (q8 or f16)")
+            raise _lib.B2AError(_lib.ERR_ARG, f"weights {weights!r} (f16, q8 or q8_dequant)")
         self.weights = weights
         T, E, H, KV, D, F = self.max_chunk, m.E, m.H, m.KV, m.D, m.F
         self.x = torch.zeros((T, E), dtype=torch.float32, device=dev)
@@ -128,8 +136,16 @@ class ChunkPrefill:
         _lib.check(lib.b2a_q8_embed(m.tok_embd.codes.data_ptr(), m.tok_embd.scales.data_ptr(),
                                     m.V, E, self.tokens.data_ptr(), T, x.data_ptr(), st))
         t_kv = pos0 + T
+        def mat(q8):  # the 16-bit rows of a Q8_0 matrix, in the reusable buffer
+            return device.q8_dequant(q8, out=self.scratch[:q8.rows * q8.cols].view(
+                q8.rows, q8.cols))
+
         for li, (ly, w) in enumerate(zip(m.layers, self.w)):
+            if self.scratch is not None:
+                w = dict(qkv=None, wo=None, gu=None, down=None, q8=w)
             h = self._norm(x, ly["attn_norm"], T)
+            if self.scratch is not None:
+                w["qkv"] = mat(w["q8"]["qkv"])
             device.gemm_qkv_rope(h, w["qkv"], pos, ch.cos, ch.sin, H=H, KV=KV,
                                  k_cache=ch.k_cache[li], v_cache=ch.v_cache[li],
                                  q_out=self.qrot[:T])
@@ -140,6 +156,11 @@ class ChunkPrefill:
                 h = self._norm(x, ly["ffn_norm"], T)
                 device.gemm_q8(h, w["gu"], out=self.act[:T], epilogue=device.GEMM_SWIGLU8)
                 device.gemm_q8(self.act[:T], w["down"], out=x, c_in=x)
+            elif self.weights == "q8_dequant":
+                device.gemm(att.view(T, qd), mat(w["q8"]["wo"]), out=x, c_in=x)
+                h = self._norm(x, ly["ffn_norm"], T)
+                device.gemm(h, mat(w["q8"]["gu"]), out=self.act[:T], epilogue=device.GEMM_SWIGLU8)
+                device.gemm(self.act[:T], mat(w["q8"]["down"]), out=x, c_in=x)
             else:
                 device.gemm(att.view(T, qd), w["wo"], out=x, c_in=x)
                 h = self._norm(x, ly["ffn_norm"], T)

@@ -707,6 +707,9 @@ def bench_prefill_chunk(dev, steps, warmup):
     pre8 = ChunkPrefill(chain, max_chunk=T, weights="q8")
     ms8 = time_chunk(pre8)
     del pre8
+    pre8d = ChunkPrefill(chain, max_chunk=T, weights="q8_dequant")
+    ms8d = time_chunk(pre8d)
+    del pre8d
     pre = ChunkPrefill(chain, max_chunk=T)
     ms = time_chunk(pre)
     E, H, KV, D, F, L = (C5["n_embd"], C5["n_head"], C5["n_kv"], C5["head_dim"], C5["n_ff"],
@@ -720,6 +723,7 @@ def bench_prefill_chunk(dev, steps, warmup):
             "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_chunk": round(ms, 3),
             "tflops": round(tf, 1), "steps": n, "weights": "f16 copy",
             "ms_per_chunk_q8_in_kernel": round(ms8, 3),
+            "ms_per_chunk_q8_dequant_per_matrix": round(ms8d, 3),
             "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": bf16,
                          "unit": "TFLOP/s", "frac": round(tf / bf16, 4),
                          "peak_source": f"{src} (MEASURED_PEAKS.json bf16_tflops, burst)"},

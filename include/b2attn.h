@@ -410,6 +410,8 @@ int b2a_swiglu_rows(const float* gu, long long gu_row_stride, int interleaved, v
  *                    for s = a . w^T: w's rows come in 256-row groups of 128
  *                    gate rows then the matching 128 up rows (model.py:
  *                    1352-1354); out has N / 2 columns, N % 256 == 0, no c_in
+ *   B2A_GEMM_SWIGLU8 the same with w's rows in 16-row groups of 8 gate rows
+ *                    then their 8 up rows (the decode GEMV's layout), N % 16 == 0
  * a [M][lda] and w [N][ldw] of dtype (B2A_F16 / B2A_BF16), K contiguous;
  * c_in f32 [M][ldc] or NULL (may equal out for an in-place residual add);
  * out [M][ldo] of out_dtype.  Pointers 16-byte aligned; lda, ldw multiples of
@@ -467,6 +469,16 @@ int b2a_gemm_qkv_rope_q8(const void* a, long long lda, const void* codes, long l
                          const int* pos_dev, const float* cos_tab, const float* sin_tab,
                          int tab_rows, int H, int KV, int D, void* q_out, void* k_cache,
                          void* v_cache, int n_ctx, void* stream);
+
+/* Q8_0 rows to 16-bit rows on the device: out[r][k] = d[r][k/32] * code[r][k]
+ * rounded once to dtype (F16 or BF16), the element b2a_gemm_q8 feeds the
+ * tensor cores; codes and scales as b2a_gemm_q8 (rows x cols, cols a
+ * multiple of 32), out [rows][ldo], 16-byte aligned, ldo a multiple of 8.
+ * For a caller that keeps Q8_0 weights only and dequantizes each matrix into
+ * one reusable buffer just before its b2a_gemm (the dequantized values the
+ * reference computes per block inside its chunk GEMM, cuda.py:287-422). */
+int b2a_q8_dequant(const void* codes, long long ldq, const void* scales, long long lds,
+                   void* out, long long ldo, int dtype, int rows, int cols, void* stream);
 
 #ifdef __cplusplus
 }

@@ -129,6 +129,34 @@ def test_gemm_qkv_rope_q8_equals_dequantized(cuda_dev, T, E, H, KV, D, pos0, dt)
         assert torch.equal(x, y)
 
 
+@pytest.mark.parametrize("rows,cols", [(16, 32), (300, 224), (4096, 2048), (3, 8192)])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_q8_dequant_equals_host_dequantization(cuda_dev, rows, cols, dt):
+    """b2a_q8_dequant: d * code rounded once, bit for bit, into a strided view."""
+    from alpacca_open_sourced_by_jt_b200 import device
+    codes, scales = _q8(rows, cols, cuda_dev, rows + cols, subnormal=True)
+    big = torch.full((rows, cols + 24), 7.0, device=cuda_dev, dtype=dt)
+    got = device.q8_dequant((codes, scales), out=big[:, 8:8 + cols])
+    torch.cuda.synchronize()
+    assert torch.equal(got, _dequant(codes, scales, dt))
+    assert (big[:, :8] == 7).all() and (big[:, 8 + cols:] == 7).all()
+
+
+@pytest.mark.parametrize("M,F,K", [(130, 1024, 512), (2048, 8192, 2048)])
+def test_gemm_swiglu8_on_16bit_weights_equals_q8(cuda_dev, M, F, K):
+    """b2a_gemm with GEMM_SWIGLU8 on the dequantized rows gives what b2a_gemm_q8
+    gives on the codes."""
+    from alpacca_open_sourced_by_jt_b200 import device
+    codes, scales = _q8(2 * F, K, cuda_dev, M)
+    a = torch.randn((M, K), device=cuda_dev).to(torch.float16)
+    got = device.gemm(a, device.q8_dequant((codes, scales)), epilogue=device.GEMM_SWIGLU8,
+                      out_dtype=torch.float16)
+    want = device.gemm_q8(a, (codes, scales), epilogue=device.GEMM_SWIGLU8,
+                          out_dtype=torch.float16)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+
+
 def test_gemm_q8_rejects_bad_arguments(cuda_dev):
     from alpacca_open_sourced_by_jt_b200 import _lib, device
     a = torch.zeros((16, 96), device=cuda_dev, dtype=torch.float16)

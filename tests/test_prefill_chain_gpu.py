@@ -22,7 +22,7 @@ from tests.golden import cases
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("weights", ["q8", "f16"])
+@pytest.mark.parametrize("weights", ["q8", "f16", "q8_dequant"])
 @pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("split", [None, 3])
 def test_chunk_prefill_matches_reference(cuda_dev, golden, dt, split, weights):
@@ -68,16 +68,18 @@ def test_chunk_prefill_rejects_bad_requests(cuda_dev):
 
 @pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
 def test_chunk_q8_weights_equal_16bit_copy(cuda_dev, dt):
-    """The in-kernel Q8_0 decode gives the products of the 16-bit copy: the
-    same logits and K/V rows up to the residual sums' order."""
+    """The in-kernel Q8_0 decode and the per-matrix dequantization give the
+    products of the 16-bit copy: the same logits and K/V rows up to the
+    residual sums' order."""
     from alpacca_open_sourced_by_jt_b200.decode_chain import DecodeChain, LlamaQ8
     from alpacca_open_sourced_by_jt_b200.prefill_chain import ChunkPrefill
     c = cases.llama_q8_case()
     model = LlamaQ8.from_spec(c, cuda_dev)
     res = []
-    for weights in ("q8", "f16"):
+    for weights in ("q8", "f16", "q8_dequant"):
         chain = DecodeChain(model, c["n_ctx"], dt)
         logits = ChunkPrefill(chain, max_chunk=8, weights=weights)(c["tokens"][:6], 0)
         res.append((logits, chain.k_cache[1][0, :6].float().cpu().numpy()))
-    assert rel_err(res[0][0], res[1][0]) < 1e-5
-    assert max_abs_err(res[0][1], res[1][1]) < 1e-2  # one 16-bit rounding apart at most
+    for other in res[1:]:
+        assert rel_err(res[0][0], other[0]) < 1e-5
+        assert max_abs_err(res[0][1], other[1]) < 1e-2  # one 16-bit rounding apart at most
