@@ -28,6 +28,11 @@ The host logic (row ranges, gather, ordering) is independent of the device
 kernels: `partial_fn` and `combine_fn` default to the B200 kernels and can be
 replaced (the CPU tests run the "nccl" exchange on gloo ranks with the NumPy
 oracle).
+
+A ragged batch of many shorter sequences is sharded by whole sequences
+instead (no exchange at all): `place_sequences` balances the ranks' rows and
+`gather_placed` brings the outputs back in batch order where a caller wants
+them in one place.
 """
 from __future__ import annotations
 
@@ -85,6 +90,34 @@ def place_sequences(lengths, world: int) -> list[list[int]]:
         placed[r].append(i)
         loads[r] += lens[i]
     return [sorted(p) for p in placed]
+
+
+def gather_placed(out_local: torch.Tensor, placed: list[list[int]], group=None) -> torch.Tensor:
+    """A batch decoded by whole sequences per rank (place_sequences), back in
+    batch order on every rank.
+
+    out_local holds this rank's outputs, one row per sequence of
+    placed[rank] in that order.  Returns (B, ...) where row i is sequence i's
+    output.  One all_gather of equal-size blocks (each rank's rows padded to
+    the largest count); the decode itself needs no exchange, this is only for
+    callers that want every output in one place."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    if len(placed) != world:
+        raise ValueError(f"placement for {len(placed)} ranks, group of {world}")
+    mine = placed[rank]
+    if out_local.shape[0] != len(mine):
+        raise ValueError(f"{out_local.shape[0]} output rows for {len(mine)} sequences")
+    cap = max(1, max(len(p) for p in placed))
+    buf = out_local.new_zeros((cap,) + tuple(out_local.shape[1:]))
+    buf[:len(mine)] = out_local
+    parts = [torch.empty_like(buf) for _ in range(world)]
+    dist.all_gather(parts, buf, group=group)
+    out = out_local.new_empty((sum(len(p) for p in placed),) + tuple(out_local.shape[1:]))
+    for r, idx in enumerate(placed):
+        if idx:
+            out[torch.tensor(idx, device=out.device)] = parts[r][:len(idx)]
+    return out
 
 
 def _gpu_partial(q, k_shard, v_shard, lens_shard, scale, max_len, out, lse):

@@ -1,8 +1,9 @@
-"""Host logic of the long-context split decode on CPU ranks (gloo,
-world size 2 and 3): row sharding, the gather and the merge order, with the
-NumPy oracle standing in for the device kernels.  Also a failure case: a
-rank that never joins makes the others fail with a timeout instead of
-hanging."""
+"""Host logic of the multi-GPU decode on CPU ranks (gloo, world size 2 and
+3), with the NumPy oracle standing in for the device kernels: the
+long-context split (row sharding, the gather and the merge order) and the
+ragged batch sharded by whole sequences (placement and the ordered gather).
+Also a failure case: a rank that never joins makes the others fail with a
+timeout instead of hanging."""
 import math
 import os
 import socket
@@ -14,8 +15,8 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle
-from alpacca_open_sourced_by_jt_b200.longctx import (LongContextDecoder, place_sequences,
-                                                     shard_lengths, shard_rows)
+from alpacca_open_sourced_by_jt_b200.longctx import (LongContextDecoder, gather_placed,
+                                                     place_sequences, shard_lengths, shard_rows)
 
 
 def test_shard_rows_cover_exactly():
@@ -139,6 +140,51 @@ def test_split_decode_on_gloo_ranks_matches_unsharded(world):
                                       V[b, :lengths[b]].numpy(), H // KV, 0.125)
         for r in range(world):
             assert np.abs(results[r][b] - ref).max() < 1e-5
+
+
+def _placed_worker(rank, world, port, q, K, V, lengths, result_q):
+    """Config 3's layout: each rank decodes whole sequences (the oracle in
+    place of the device decode), then gathers the batch in order."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        placed = place_sequences(lengths, world)
+        H, KV = q.shape[1], K.shape[2]
+        mine = [oracle.attention_decode(q[b].numpy(), K[b, :lengths[b]].numpy(),
+                                        V[b, :lengths[b]].numpy(), H // KV, 0.125)
+                for b in placed[rank]]
+        local = torch.from_numpy(np.stack(mine)) if mine else torch.zeros((0,) + q.shape[1:])
+        result_q.put((rank, gather_placed(local, placed).numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sequence_placed_batch_on_gloo_ranks_matches_unsharded(world):
+    rng = np.random.default_rng(60 + world)
+    B, H, KV, D, L = 7, 8, 2, 16, 40
+    q = torch.from_numpy(rng.standard_normal((B, H, D), dtype=np.float32))
+    K = torch.from_numpy(rng.standard_normal((B, L, KV, D), dtype=np.float32))
+    V = torch.from_numpy(rng.standard_normal((B, L, KV, D), dtype=np.float32))
+    lengths = [40, 3, 17, 29, 1, 33, 8]
+    ctx = mp.get_context("spawn")
+    rq = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_placed_worker, args=(r, world, port, q, K, V, lengths, rq))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(rq.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for b in range(B):
+        ref = oracle.attention_decode(q[b].numpy(), K[b, :lengths[b]].numpy(),
+                                      V[b, :lengths[b]].numpy(), H // KV, 0.125)
+        for r in range(world):
+            assert np.array_equal(results[r][b], ref.astype(np.float32))
 
 
 def _lonely_worker(port, result_q):
