@@ -12,7 +12,8 @@
 //
 // SWIGLU takes the FFN's gate and up weights interleaved in 128-row groups
 // (gate rows 128g..128g+127, then the matching up rows) and writes the
-// activation the down projection reads (model.py:1352-1354).
+// activation the down projection reads (model.py:1352-1354); SWIGLU8 (epilogue
+// 4) takes the decode GEMV's 16-row groups of 8 gate rows then 8 up rows.
 //
 // QKV_ROPE (b2a_gemm_qkv_rope) takes w = [Wq; Wk; Wv] and writes q rotated
 // (16-bit) plus the rotated k and the v rows at each token's cache position,
