@@ -112,6 +112,8 @@ def test_gemm_rejects_bad_arguments(cuda_dev):
     with pytest.raises(_lib.B2AError):
         device.gemm(a, w[:100], epilogue=device.GEMM_SWIGLU)  # N % 256
     with pytest.raises(_lib.B2AError):
+        device.gemm(a, w[:40], epilogue=device.GEMM_SWIGLU8)  # N % 16
+    with pytest.raises(_lib.B2AError):
         device.gemm(a, w.to(torch.float16))  # mixed operand types
     lib = _lib.load()
     assert lib.b2a_gemm(a.data_ptr(), 60, w.data_ptr(), 64, _lib.BF16, None, 0,
