@@ -10,13 +10,13 @@ bytes (B*2*L*KV*D*2 per rank, all ranks) / max-over-ranks device time.
 The caches (2.15 GB per rank) exceed the 126 MB L2, so no flush is needed.
 
 Also reported on the same line:
-  prefill   BASELINE config 2 causal prefill (S=2048, 32/8 heads, D=128,
+  prefill   benchmark config 2 causal prefill (S=2048, 32/8 heads, D=128,
             bf16 in/out) in TFLOP/s, flops = 4*H*D*S(S+1)/2, L2 flushed
             between launches (inputs are 24 MB)
-  varlen    BASELINE config 3: one batch of 64 sequences of ragged length
+  varlen    benchmark config 3: one batch of 64 sequences of ragged length
             (1K-8K), sharded by sequence over the GPUs, fp16 KV, fused
             RoPE+append then decode, GB/s
-  longctx   BASELINE config 4: 4 x 131072 rows split over the GPUs; one CUDA
+  longctx   benchmark config 4: 4 x 131072 rows split over the GPUs; one CUDA
             graph per step: local split-KV decode, then one kernel that
             exchanges the ranks' (o, lse) rows over NVLink peer memory and
             merges them (the NCCL all-gather path and the one-GPU decode
@@ -25,7 +25,7 @@ Also reported on the same line:
             layer (HBM GB/s) and a whole-layer f32 snapshot
   qwen35_layer  Qwen35 full-attention layer step (prologue, decode, gate) at
             16 x 32K rows, 16/2 heads, head_dim 256, bf16, GB/s
-  decode_step  BASELINE config 5: a whole decode token of a 16-layer Q8_0
+  decode_step  benchmark config 5: a whole decode token of a 16-layer Q8_0
             llama decoder as one CUDA graph, tokens/s (device and e2e)
   prefill_chunk  a 2048-token prefill chunk of the same model kept on the
             device, tokens/s and TFLOP/s
@@ -240,7 +240,7 @@ def _timed_steps(fn, nsteps, dev, dist):
 
 
 def bench_longctx(dev, rank, world, steps, warmup, dist):
-    """4 sequences x 131072 rows, 64 q / 8 KV heads, D=128,
+    """benchmark config 4: 4 sequences x 131072 rows, 64 q / 8 KV heads, D=128,
     bf16; the KV rows of every sequence are split across the ranks (strong
     scaling).  One step, replayed as a CUDA graph: the split-KV decode of the
     rank's rows, then b2a_decode_sharded's fused kernel (split merge, NVLink
@@ -315,7 +315,7 @@ def bench_longctx(dev, rank, world, steps, warmup, dist):
 
 
 def bench_varlen(dev, rank, world, steps, warmup, dist):
-    """one batch of 64 sequences with cached lengths
+    """benchmark config 3: one batch of 64 sequences with cached lengths
     L_b ~ U[1024, 8192] (seed 2), 32 q / 8 KV heads, D=128, fp16 KV ~ N(0,1)
     (seed 2 + rank), sharded by sequence over the GPUs (longctx.place_sequences:
     longest first onto the rank with the fewest rows; no collective).  One step is the device half of
@@ -526,7 +526,7 @@ C5 = dict(n_layer=16, n_embd=2048, n_head=32, n_kv=8, head_dim=64, n_ff=8192, n_
 
 
 def bench_decode_step(dev, steps, warmup):
-    """a whole decode token of a random-init 16-layer
+    """benchmark config 5: a whole decode token of a random-init 16-layer
     llama decoder (hidden 2048, 32/8 heads of 64, FFN 8192 SwiGLU, vocab
     128256, RMSNorm 1e-5) with Q8_0 weights N(0, 0.02) (seed 5), an fp16 KV
     cache holding a full 4096-row context, batch 1, the token replayed as one
@@ -984,7 +984,7 @@ def run_ours(args):
             result["prefill"] = {
                 "metric": "prefill-attn TFLOPS", "value": round(pf["tflops"], 1),
                 "unit": "TFLOP/s", "ms_per_launch": round(pf["ms"], 4),
-                "config": "BASELINE config 2: S=2048 causal, 32 q / 8 KV heads, D=128, bf16 "
+                "config": "benchmark config 2: S=2048 causal, 32 q / 8 KV heads, D=128, bf16 "
                           "in/out, fp32 accumulation; L2 flushed before each launch",
                 "roofline": {"bound": "tensor", "achieved": round(pf["tflops"], 1),
                              "peak": bf16, "unit": "TFLOP/s",

@@ -2,7 +2,7 @@
 
 Every case returns its arrays plus `sha256`, a digest of the input bytes, so
 a test can check that it regenerated exactly the inputs the golden file was
-made from.  Shapes follow BASELINE.json's configs (config 1 exactly; the
+made from.  Shapes follow the benchmark configurations (config 1 exactly; the
 others at sizes a CPU finishes in seconds).
 """
 from __future__ import annotations
@@ -25,7 +25,7 @@ def _digest(*arrays) -> str:
 
 
 def decode_config1():
-    """batch 1, 32 query / 8 KV heads, head_dim 64,
+    """benchmark config 1: batch 1, 32 query / 8 KV heads, head_dim 64,
     context 512, fp32, Q/K/V ~ N(0,1) seed 0, RoPE theta 500000 ("norm",
     llama) on K positions 0..511 and q at 511, scale 1/sqrt(64)."""
     H, KV, D, L = 32, 8, 64, 512

@@ -1,4 +1,4 @@
-"""BASELINE config 5 at its full size: the benchmarked model against the oracle.
+"""benchmark config 5 at its full size: the benchmarked model against the oracle.
 
 The model is the one bench.py's decode_step leg times: LlamaQ8.random with
 16 layers, hidden 2048, 32 q / 8 KV heads of 64, SwiGLU FFN 8192, vocab

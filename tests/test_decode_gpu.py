@@ -51,7 +51,7 @@ def _run(B, H, KV, D, lens, dt, dev, split_rows=0, n_ctx=None, pad=0, seed=0, ls
 
 
 def test_config1_golden_through_dropin(cuda_dev, golden):
-    """BASELINE config 1 end to end through kernels.attention_decode (the
+    """benchmark config 1 end to end through kernels.attention_decode (the
     reference's kernels.py signature) against the reference's own output."""
     from alpacca_open_sourced_by_jt_b200 import kernels
     g = golden("decode_config1.npz")

@@ -1,4 +1,4 @@
-"""Decode at BASELINE's full sizes, checked through properties that hold at
+"""Decode at the benchmark's full sizes, checked through properties that hold at
 any size (the oracle's NumPy einsum would take minutes there):
 
 * the headline workload (16 sequences x 32768 rows, 32 q / 8 KV heads,

@@ -1,4 +1,4 @@
-"""BASELINE's 16-bit configurations at full size against a plain PyTorch fp32
+"""the benchmark's 16-bit configurations at full size against a plain PyTorch fp32
 reference of the same attention, computed on the GPU.
 
 The CPU oracle would take minutes at these sizes; the fp32 reference here

@@ -52,7 +52,7 @@ class StandInModel:
 
 
 def test_config1_decode_steps_through_hooks(cuda_dev, golden):
-    """BASELINE config 1 as the engine runs it: each cached K row rotated by
+    """benchmark config 1 as the engine runs it: each cached K row rotated by
     the hooked _rope_np at its position, the query at 511, then the hooked
     _attention_np over the cache, plus a few earlier decode steps."""
     from alpacca_open_sourced_by_jt_b200 import model_hooks

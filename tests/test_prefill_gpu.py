@@ -76,7 +76,7 @@ def test_16bit_output(cuda_dev, kernel, out_dtype):
 
 
 def test_config2_shape(cuda_dev, kernel):
-    """BASELINE config 2 geometry (S=2048, 32/8 heads, D=128, bf16, bf16 out)
+    """benchmark config 2 geometry (S=2048, 32/8 heads, D=128, bf16, bf16 out)
     against the oracle on a subset of heads' rows (the oracle's fp32 einsum
     over all 32 heads x 2048^2 scores is too slow for a unit test)."""
     from alpacca_open_sourced_by_jt_b200 import device
