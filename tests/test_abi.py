@@ -159,3 +159,33 @@ def test_qwen35_layer_entries_reject_bad_arguments(lib):
     assert lib.b2a_sigmoid_gate(p, 64, p, 128, p, 64, 0, 64, None) == _lib.OK
     assert lib.b2a_sigmoid_gate(None, 64, p, 128, p, 64, 4, 64, None) == _lib.ERR_ARG
     assert lib.b2a_sigmoid_gate(p, 32, p, 128, p, 64, 4, 64, None) == _lib.ERR_SHAPE
+
+
+def test_q8_gemm_entry_points_reject_bad_arguments(lib):
+    """Host-side checks of the Q8_0 GEMM / dequantize entry points and of the
+    SWIGLU8 epilogue (every rejection returns before any CUDA call)."""
+    p = 1 << 20
+    # b2a_gemm_q8(a, lda, codes, ldq, scales, lds, dtype, c_in, ldc, out, ldo, out_dtype,
+    #             M, N, K, epilogue, stream)
+    ok = [p, 96, p, 96, p, 3, _lib.F16, None, 0, p, 64, _lib.F32, 16, 64, 96, 0, None]
+    for i, v, code in ((2, None, _lib.ERR_ARG),        # no codes
+                       (14, 80, _lib.ERR_SHAPE),       # K not a multiple of 32
+                       (3, 88, _lib.ERR_ALIGN),        # code rows not 16 bytes apart
+                       (5, 2, _lib.ERR_ALIGN),         # scales row shorter than K/32
+                       (4, p + 1, _lib.ERR_ALIGN),     # scales not 2-byte aligned
+                       (15, 9, _lib.ERR_ARG),          # epilogue
+                       (6, _lib.F32, _lib.ERR_DTYPE)):  # operand type
+        bad = list(ok)
+        bad[i] = v
+        assert lib.b2a_gemm_q8(*bad) == code, (i, v)
+    bad = list(ok)
+    bad[13], bad[15] = 40, 2  # SWIGLU8 with rows not a multiple of 16
+    assert lib.b2a_gemm_q8(*bad) == _lib.ERR_SHAPE
+    # b2a_q8_dequant(codes, ldq, scales, lds, out, ldo, dtype, rows, cols, stream)
+    assert lib.b2a_q8_dequant(p, 64, p, 2, None, 64, _lib.F16, 8, 64, None) == _lib.ERR_ARG
+    assert lib.b2a_q8_dequant(p, 64, p, 2, p, 64, _lib.F16, 8, 48, None) == _lib.ERR_SHAPE
+    assert lib.b2a_q8_dequant(p, 64, p, 2, p, 60, _lib.F16, 8, 64, None) == _lib.ERR_ALIGN
+    assert lib.b2a_q8_dequant(p, 64, p, 2, p + 8, 64, _lib.F16, 8, 64, None) == _lib.ERR_ALIGN
+    # b2a_gemm with SWIGLU8 and rows not a multiple of 16
+    assert lib.b2a_gemm(p, 64, p, 64, _lib.BF16, None, 0, p, 64, _lib.F32, 16, 40, 64, 2,
+                        None) == _lib.ERR_SHAPE
